@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Isosurface throughput on B200: input Gcells/s of flying-edges marching cubes.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tack_b200|reference]
+
+Workload (default): 1024^3 f32 volume, sum of 32 seeded Gaussian blobs,
+isovalue 0.5 -- the configuration the metric is quoted on at 1/2/4/8 GPUs.
+The volume is z-slab sharded across N GPUs (one process per GPU, launched by
+torchrun for N > 1): each rank classifies/counts/scans its slab, one NCCL
+all-gather exchanges the per-rank totals, each rank emits its slices of the
+single-volume output.  Total work is fixed as N grows (strong scaling).
+
+A step = one isosurface of the whole volume from resident f32 values to
+resident points + connectivity, including the host read of the totals and the
+exact-size output allocation.  `value` = cells of the whole volume per second
+over K timed steps (CUDA events, max over ranks).  `e2e` = the same metric
+through the public API from pinned host memory: each step copies the volume
+host->device, runs flying_edges, copies points and connectivity back.
+
+The reference arm (--impl reference) times the CPU parity oracle -- a C
+restatement of the reference's flying-edges kernels with its host
+orchestration, using every host core -- on a bounded z-slab of the same
+volume (the reference itself is a Python package whose JIT path cannot be
+shipped to the GPU host).
+"""
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+if REPO not in sys.path:
+    sys.path.insert(0, REPO)
+
+METRIC = "isosurface input Gcells/s at 1/2/4/8 B200; achieved HBM GB/s vs peak"
+TRAFFIC_FILE = os.path.join(REPO, "profiles", "fe_threshold_blobs1024.txt")
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="tack_b200", choices=["tack_b200", "reference"])
+    ap.add_argument("--config", default="blobs")
+    ap.add_argument("--size", type=int, nargs=3, default=None,
+                    help="override the volume's node counts (nx ny nz)")
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    return 6650.0, "fallback (6.65 TB/s, earlier measurement on this pool)"
+
+
+def committed_traffic():
+    """DRAM bytes per launch of the threshold kernel from the committed ncu
+    summary (a line 'dram_bytes_per_launch_1024cubed: N'), or None."""
+    if not os.path.exists(TRAFFIC_FILE):
+        return None
+    for line in open(TRAFFIC_FILE):
+        if line.startswith("dram_bytes_per_launch_1024cubed:"):
+            return float(line.split(":", 1)[1].split()[0])
+    return None
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.dev = device_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        import tempfile
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.dev)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"samples": 0, "note": "nvidia-smi unavailable"}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- reference arm
+
+def cpu_sample_rate(volume_host_planes, shape, k0, nthreads, min_seconds, max_calls=50):
+    """Oracle flying_edges on a z-slab; returns (Gcells/s, per-call seconds, cells)."""
+    from oracle import oracle
+    nx, ny, _ = shape
+    nz_cells = volume_host_planes.size // (nx * ny) - 1
+    g = oracle.Grid(nx - 1, ny - 1, nz_cells, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0)
+    cells = (nx - 1) * (ny - 1) * nz_cells
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        oracle.flying_edges(volume_host_planes, g, 0.5, nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+        if (time.perf_counter() - t_start >= min_seconds and len(times) >= 3) or \
+                len(times) >= max_calls:
+            break
+    t = statistics.median(times)
+    return cells / t / 1e9, t, cells
+
+
+def host_slab(args, shape, planes, device):
+    """The middle `planes` node planes of the workload, as a host array."""
+    from tack_b200 import workloads
+    nz = shape[2]
+    k0 = max(0, nz // 2 - planes // 2)
+    v = workloads.generate(args.config, shape, k0, k0 + planes, device=device)
+    return v.cpu().numpy(), k0
+
+
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+    from oracle import oracle
+    from tack_b200 import workloads
+    oracle.build()
+    cfg = workloads.CONFIGS[args.config]
+    shape = tuple(args.size) if args.size else cfg["shape"]
+    device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    nthreads = oracle.num_threads(0)
+    # Size the slab so that warmup + steps fit in about two minutes.
+    calib, k0 = host_slab(args, shape, 8, device)
+    rate, _, _ = cpu_sample_rate(calib, shape, k0, nthreads, 0.0, max_calls=2)
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    cells_per_plane = (shape[0] - 1) * (shape[1] - 1)
+    planes = int(np.clip(budget * rate * 1e9 / cells_per_plane, 2, min(128, shape[2])))
+    vol, k0 = host_slab(args, shape, planes, device)
+    nz_cells = planes - 1
+    g = oracle.Grid(shape[0] - 1, shape[1] - 1, nz_cells, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0)
+    cells = cells_per_plane * nz_cells
+    for _ in range(args.warmup):
+        oracle.flying_edges(vol, g, cfg["isovalues"][0], nthreads=nthreads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.flying_edges(vol, g, cfg["isovalues"][0], nthreads=nthreads)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = cells * args.steps / total / 1e9
+    sample = (f"node planes [{k0},{k0 + planes}) of the {shape[0]}x{shape[1]}x{shape[2]} "
+              f"{args.config} volume ({cells} cells) per step")
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcells/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": total / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args.config, shape, cfg["isovalues"]),
+                   "volume_nodes": list(shape), "isovalues": cfg["isovalues"]},
+        "cpu_baseline": {"value": value, "unit": "Gcells/s", "cores": nthreads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "Gcells/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": ("CPU parity oracle (C restatement of the reference's flying-edges kernels "
+                 "and host orchestration, pthreads over rows), all host threads"),
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def workload_name(config, shape, isos):
+    desc = {"blobs": "sum of 32 seeded Gaussian blobs", "gyroid": "gyroid + N(0,0.01) noise",
+            "sines": "sum of 8 seeded sinusoids", "sphere": "sphere SDF",
+            "noise": "4-octave value noise"}[config]
+    return (f"flying-edges isosurface, {shape[0]}x{shape[1]}x{shape[2]} f32 volume, {desc}, "
+            f"isovalue(s) {isos}")
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import torch.distributed as dist
+
+    import tack_b200 as tack
+    from tack_b200 import _lib, workloads
+    from tack_b200.distributed import SlabEngine, SlabPlan, slab_bases
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    tack.init(tack.cuda, device=local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    cfg = workloads.CONFIGS[args.config]
+    shape = tuple(args.size) if args.size else cfg["shape"]
+    isos = cfg["isovalues"]
+    nxn, nyn, nzn = shape
+    plan = SlabPlan(nzn, world, rank)
+    grid = tack.UniformGrid(nxn - 1, nyn - 1, nzn - 1, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+    vol = workloads.generate(args.config, shape, plan.k0, plan.k1, device=dev)
+    torch.cuda.synchronize()
+    eng = SlabEngine(grid, plan, isos)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    niso = len(isos)
+    isoc = (ctypes_f32(isos))
+    local_nodes = vol.numel()
+    cells = (nxn - 1) * (nyn - 1) * (nzn - 1)
+
+    ev = {}
+
+    def step(i=None):
+        # K1: one read of the slab -> node bitmasks
+        if i is not None:
+            ev["a"][i].record(stream)
+        _lib.check(lib.tkmc_fe_classify(vol.data_ptr(), grid.nx, grid.ny, plan.nz_cells, isoc,
+                                        niso, eng.ws.data_ptr(), eng.nbytes,
+                                        stream.cuda_stream), "classify")
+        if i is not None:
+            ev["b"][i].record(stream)
+        # K2: counts + single-pass scan; host read of the totals
+        _lib.check(lib.tkmc_fe_scan(grid.nx, grid.ny, plan.nz_cells, 1 if plan.ghost else 0,
+                                    niso, None, eng.ws.data_ptr(), eng.nbytes,
+                                    stream.cuda_stream), "scan")
+        if i is not None:
+            ev["c"][i].record(stream)
+        counts = np.zeros(niso * 4, np.int64)
+        _lib.check(lib.tkmc_fe_read_counts(grid.nx, grid.ny, plan.nz_cells, niso,
+                                           eng.ws.data_ptr(), eng.nbytes, counts.ctypes.data,
+                                           stream.cuda_stream), "read_counts")
+        counts = counts.reshape(niso, 4)
+        allc = eng.exchange(counts)
+        b = slab_bases(allc, rank)
+        if i is not None:
+            ev["d"][i].record(stream)
+        pts, conn = eng.emit(vol, counts, b)  # K3 (+ exact-size allocation)
+        if i is not None:
+            ev["e"][i].record(stream)
+        return counts, b, pts, conn
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    K = args.steps
+    for key in "abcde":
+        ev[key] = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    barrier()
+    clocks.start()
+    launches0 = lib.tkmc_launch_count()
+    t_start.record(stream)
+    for i in range(K):
+        counts, bases, pts, conn = step(i)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = lib.tkmc_launch_count() - launches0
+    clk = clocks.stop()
+    barrier()
+    ms = t_start.elapsed_time(t_end)
+    k1 = sum(ev["a"][i].elapsed_time(ev["b"][i]) for i in range(K)) / K
+    k2 = sum(ev["b"][i].elapsed_time(ev["c"][i]) for i in range(K)) / K
+    k3 = sum(ev["d"][i].elapsed_time(ev["e"][i]) for i in range(K)) / K
+    host = sum(ev["c"][i].elapsed_time(ev["d"][i]) for i in range(K)) / K
+    stats = torch.tensor([ms, k1, k2, k3, host], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    ms, k1, k2, k3, host = (float(x) for x in stats.cpu())
+    total_points = int(bases["totals"][:, 0].sum())
+    total_tris = int(bases["totals"][:, 1].sum())
+
+    # ---- e2e through the public API, host buffers -------------------------
+    e2e = None
+    if not args.no_e2e and args.e2e_steps > 0:
+        e2e = run_e2e(args, tack, torch, dist, vol, grid, plan, eng, isos, world, rank, dev,
+                      cells)
+
+    # ---- CPU baseline (oracle, host cores), N == 1 only ------------------------
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        from oracle import oracle
+        oracle.build()
+        nthreads = oracle.num_threads(0)
+        planes = min(64, nzn)
+        k0 = max(0, nzn // 2 - planes // 2)
+        slab = vol.view(nzn, nyn, nxn)[k0:k0 + planes].reshape(-1).cpu().numpy()
+        rate, t_call, scells = cpu_sample_rate(slab, shape, k0, nthreads, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "Gcells/s", "cores": nthreads, "kind": "port",
+               "sample": (f"node planes [{k0},{k0 + planes}) of the same volume "
+                          f"({scells} cells), median of repeated calls over "
+                          f">= {args.cpu_seconds:.0f} s"),
+               "seconds_per_call": t_call}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        peak, peak_src = measured_peaks()
+        alg_k1 = 4.0 * local_nodes  # one read of this rank's slab (incl. ghost)
+        achieved = alg_k1 / (k1 * 1e-3) / 1e9
+        traffic = committed_traffic()
+        if traffic is not None:
+            traffic = traffic * local_nodes / float(1024 ** 3)
+        step_bytes = 4.0 * nxn * nyn * nzn + 12.0 * (total_points + total_tris)
+        value = cells * K / (ms * 1e-3) / 1e9
+        out = {
+            "metric": METRIC, "value": value, "unit": "Gcells/s", "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": ms / K,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {
+                "workload": workload_name(args.config, shape, isos),
+                "volume_nodes": list(shape), "cells": cells, "isovalues": isos,
+                "parallelism": (f"z-slab x{world} (ghost plane, one NCCL all-gather of totals)"
+                                if world > 1 else "single GPU"),
+                "l2": "inputs larger than L2 (f32 volume 4 GiB >> 126 MB L2), no flush",
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "k_fe_threshold (K1: volume -> node bitmask)",
+                "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic, "peak_source": peak_src,
+                "algorithmic_bytes_per_launch": alg_k1,
+                "launch_ms": k1,
+            },
+            "step_roofline": {
+                "algorithmic_bytes": step_bytes,
+                "achieved_gbs": step_bytes / (ms / K * 1e-3) / 1e9,
+                "frac_of_aggregate_peak": step_bytes / (ms / K * 1e-3) / 1e9 / (peak * world),
+            },
+            "kernels_ms": {"k1_threshold": k1, "k2_count_scan": k2,
+                           "host_counts_exchange_bases": host, "k3_emit_incl_alloc": k3},
+            "outputs": {"points": total_points, "triangles": total_tris},
+            "gpu_launches": int(launches),
+            "gpu_launches_per_step": launches / K,
+            "clocks": clk,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def ctypes_f32(vals):
+    import ctypes
+    return (ctypes.c_float * len(vals))(*vals)
+
+
+def run_e2e(args, tack, torch, dist, vol, grid, plan, eng, isos, world, rank, dev, cells):
+    """Public API from pinned host memory: H2D volume, isosurface, D2H result."""
+    host = torch.empty(vol.numel(), dtype=torch.float32, pin_memory=True)
+    host.copy_(vol)
+    dvol = torch.empty_like(vol)
+    stream = torch.cuda.current_stream(dev)
+    d2h = 0
+    h2d = host.numel() * 4
+
+    def once():
+        nonlocal d2h
+        dvol.copy_(host, non_blocking=True)
+        if world == 1:
+            r = tack.flying_edges(tack.from_torch(dvol), grid, isos if len(isos) > 1 else isos[0])
+            d2h = r["points"].nbytes + r["conn"].nbytes
+        else:
+            r = eng.run(dvol)
+            p = r["points_field"].tensor.cpu()
+            c = r["conn_field"].tensor.cpu()
+            d2h = p.numel() * 4 + c.numel() * 4
+        return r
+
+    once()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.e2e_steps):
+        once()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = torch.tensor([t0.elapsed_time(t1)], dtype=torch.float64, device=dev)
+    tot = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tot)
+    ms = float(ms.item())
+    return {"value": cells * args.e2e_steps / (ms * 1e-3) / 1e9, "unit": "Gcells/s",
+            "h2d_bytes_per_step": int(tot[0].item()), "d2h_bytes_per_step": int(tot[1].item()),
+            "ms_per_step": ms / args.e2e_steps, "steps": args.e2e_steps,
+            "path": ("tack_b200.flying_edges (pinned host -> device volume copy, "
+                     "points/conn copied back to numpy)" if world == 1 else
+                     "tack_b200.distributed SlabEngine.run per rank + D2H of its slices")}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,210 @@
+/*
+ * tackmc.h -- C ABI of libtackmc.so, the sm_100a isosurface library behind
+ * tack_b200.algorithms.flying_edges.
+ *
+ * Every entry point takes plain pointers, 64-bit sizes and a CUDA stream
+ * passed as `void*` (NULL = legacy default stream).  Device pointers must
+ * belong to the device that is current on the calling thread.  No entry
+ * point allocates or frees device memory: scratch space is a caller-provided
+ * workspace whose size the matching *_workspace_bytes() function returns.
+ * Every entry point returns an int status (TKMC_OK == 0); on failure
+ * tkmc_last_error() returns a thread-local message.  Nothing exits, traps or
+ * waits without a bound.
+ *
+ * Reference interfaces replaced (paths inside berkgeveci/tack):
+ *   packages/tack-vis/src/tack/algorithms/flying_edges.py
+ *   packages/tack-core/src/tack/algorithms/scan.py
+ *   packages/tack-core/src/tack/runtime/cuda_backend.py
+ *   packages/tack-vis/examples/26_marching_cubes.py
+ */
+#ifndef TACKMC_H
+#define TACKMC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define TKMC_OK                  0
+#define TKMC_ERR_INVALID_ARG     1  /* bad size, null pointer, misuse          */
+#define TKMC_ERR_WORKSPACE       2  /* workspace smaller than required         */
+#define TKMC_ERR_OVERFLOW        3  /* point total does not fit int32 ids      */
+#define TKMC_ERR_DEVICE_TIMEOUT  4  /* a bounded device-side wait expired      */
+#define TKMC_ERR_CUDA            5  /* CUDA runtime error (message has detail) */
+#define TKMC_ERR_CAPACITY        6  /* caller's output buffers too small       */
+
+/* Largest number of isovalues one fe call classifies in a single volume read. */
+#define TKMC_MAX_ISO 8
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int tkmc_version(void);
+
+/* Thread-local message describing the last failed call on this thread. */
+const char* tkmc_last_error(void);
+
+/* Number of kernels this library has launched in this process (all devices).
+ * Used by benchmarks to count their own launches inside a timed region. */
+uint64_t tkmc_launch_count(void);
+
+/* Host-only: copy the marching-cubes case tables the kernels use into host
+ * arrays: tri_table[256*16] (edge ids, -1 padded), num_tris[256],
+ * edge_corners[24].  Any pointer may be NULL.
+ * Replaces: flying_edges.py:33-306 (_EDGE_CORNERS, _TRI_TABLE, _NUM_TRIS) and
+ * flying_edges.py:344-371 (MCTables / _get_tables). */
+int tkmc_mc_tables(int32_t* tri_table, int32_t* num_tris, int32_t* edge_corners);
+
+/* ---- field reductions --------------------------------------------------- */
+
+/* Workspace for tkmc_reduce_f32 over n values. */
+size_t tkmc_reduce_workspace_bytes(int64_t n);
+
+/* min, max and sum of n f32 values in one read, written to HOST out4 as
+ * doubles {min, max, sum, nan_count}.  min/max ignore NaN (CUDA fminf/fmaxf
+ * semantics); all-NaN or n == 0 gives min = +inf, max = -inf.  The sum is
+ * accumulated in f64 in a fixed order (deterministic for a given device).
+ * Synchronises `stream`.
+ * Replaces: cuda_backend.py:576-615 (CUDABackend.reduce_field) and the
+ * reduce_sum/min/max_f32 kernels at cuda_backend.py:44-106, whose element
+ * count is a 32-bit uint (cuda_backend.py:49); n here is 64-bit. */
+int tkmc_reduce_f32(const float* values, int64_t n, void* workspace,
+                    size_t workspace_bytes, double* out4, void* stream);
+
+/* ---- prefix scan -------------------------------------------------------- */
+
+/* Workspace for tkmc_scan_i32 over n values. */
+size_t tkmc_scan_workspace_bytes(int64_t n);
+
+/* Single-pass (decoupled look-back) prefix sum of n int32 values.
+ * inclusive == 0: out[i] = sum(in[0..i-1]), out[0] = 0;  inclusive != 0:
+ * out[i] = sum(in[0..i]).  Sums are carried in int64 and stored as int32
+ * (two's-complement wrap, as the reference's int32 fields do); *total (HOST,
+ * may be NULL) receives the exact int64 sum of all n values.  `in` and `out`
+ * may alias.  Synchronises `stream` when total != NULL.
+ * Replaces: scan.py:81-102 (exclusive_scan) and scan.py:105-123
+ * (inclusive_scan). */
+int tkmc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive,
+                  void* workspace, size_t workspace_bytes, int64_t* total,
+                  void* stream);
+
+/* ---- flying edges (merged-point marching cubes) ------------------------- */
+/*
+ * Grid: nx, ny, nz cells; (nx+1)*(ny+1)*(nz+1) f32 node values, i fastest,
+ * k slowest (flying_edges.py:313-341 UniformGrid).  Cells with mask[cell] != 0
+ * emit no triangles (mask is nullable; int32 per cell, flying_edges.py:441-477).
+ *
+ * ghost_plane != 0 marks node plane nz as a read-only ghost owned by the next
+ * z-slab: its nodes close this slab's last cell layer, but its x/y edges are
+ * not counted in this slab's totals (they belong to the next slab, whose
+ * point-id bases make the ids match).  Single-volume calls pass 0.
+ *
+ * Output layout is the reference's (flying_edges.py:480-656): all x-edge
+ * points in node-row order, then all y-edge points, then all z-edge points;
+ * triangles in cell-row order, tri-table order within a cell; points f32
+ * [x,y,z] interleaved, conn int32 triples.  For several isovalues each
+ * isovalue's block follows the previous one.
+ */
+
+/* Workspace for the fe calls on this grid and number of isovalues. */
+size_t tkmc_fe_workspace_bytes(int64_t nx, int64_t ny, int64_t nz, int niso);
+
+/* Pass 1 (count): classify every node against each isovalue in ONE read of
+ * the volume, count x/y/z edge crossings per node row and triangles per cell
+ * row, and scan them into per-row offsets kept in the workspace.  Writes
+ * HOST counts[niso*4] = {X, Y, Z, T} per isovalue (this slab's own totals).
+ * Synchronises `stream`.
+ * Replaces: flying_edges.py:663-715 (_count_block: _fe_count_edges_xyz,
+ * _fe_count_rows, to_numpy and numpy cumsum). */
+int tkmc_fe_count(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                  int ghost_plane, const float* isovalues, int niso,
+                  const int32_t* mask, void* workspace, size_t workspace_bytes,
+                  int64_t* counts, void* stream);
+
+/* Pass 2 (emit): write points and connectivity using the offsets left in the
+ * workspace by tkmc_fe_count (same arguments).  Per isovalue q:
+ *   pt_id_base[3q+s]  is added to section-s (0=x,1=y,2=z) offsets to form the
+ *                     point ids stored in conn;
+ *   pt_out_base[3q+s] is added to the same offsets to form the row index in
+ *                     `points` where section-s points are written;
+ *   tri_out_base[q]   is the row index in `conn` of q's first triangle.
+ * For one volume: pt_id_base = pt_out_base = {P0, P0+X, P0+X+Y} with P0 the
+ * points of earlier isovalues, tri_out_base = earlier triangles.  geom6 =
+ * {x0, y0, z0, dx, dy, dz}; k_offset is the global index of this slab's node
+ * plane 0 (point z uses float(k + k_offset), exactly as the reference).
+ * Asynchronous on `stream`.
+ * Replaces: flying_edges.py:718-746 (_emit_block: _fe_emit_points_xyz,
+ * _fe_emit_tris). */
+int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                 int ghost_plane, int64_t k_offset, const float* geom6,
+                 const float* isovalues, int niso, const int32_t* mask,
+                 void* workspace, size_t workspace_bytes,
+                 const int64_t* pt_id_base, const int64_t* pt_out_base,
+                 const int64_t* tri_out_base, float* points, int32_t* conn,
+                 void* stream);
+
+/* Phase entry points of tkmc_fe_count, for callers that time or overlap the
+ * phases.  classify = one volume read -> node bitmasks (asynchronous);
+ * scan = counts + offsets from the bitmasks (asynchronous);
+ * read_counts = copy counts to HOST and check the device error word
+ * (synchronises).  classify + scan + read_counts == tkmc_fe_count. */
+int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                     const float* isovalues, int niso, void* workspace,
+                     size_t workspace_bytes, void* stream);
+int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                 int niso, const int32_t* mask, void* workspace,
+                 size_t workspace_bytes, void* stream);
+int tkmc_fe_read_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
+                        void* workspace, size_t workspace_bytes,
+                        int64_t* counts, void* stream);
+
+/* Copy to HOST the per-node-row exclusive offsets that the last
+ * tkmc_fe_count / tkmc_fe_scan left in the workspace for isovalue `iso`:
+ * out[4*r + s], s = 0..3: x, y, z point offsets (each relative to its own
+ * section) and triangle offset of node row r = k*(ny+1) + j (the triangle
+ * offset of the cell row (j, k) when j < ny and k < nz).  (ny+1)*(nz+1)
+ * rows.  Synchronises `stream`.
+ * Replaces the xo/yo/zo/tri_offsets arrays of flying_edges.py:693-715
+ * (_count_block); those add the x total to yo and x+y totals to zo. */
+int tkmc_fe_row_offsets(int64_t nx, int64_t ny, int64_t nz, int niso, int iso,
+                        const void* workspace, size_t workspace_bytes,
+                        int64_t* out, void* stream);
+
+/* Whole filter for one volume into caller buffers of fixed capacity:
+ * count, then emit if points_capacity >= sum of points and conn_capacity >=
+ * sum of triangles (capacities in rows of 3).  counts as in tkmc_fe_count.
+ * Returns TKMC_ERR_CAPACITY (with counts filled, nothing emitted) when the
+ * buffers are too small, so the caller can grow them and call tkmc_fe_emit.
+ * Replaces: flying_edges.py:749-763 (flying_edges) for C callers. */
+int tkmc_fe_run(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                const float* geom6, const float* isovalues, int niso,
+                const int32_t* mask, void* workspace, size_t workspace_bytes,
+                float* points, int64_t points_capacity, int32_t* conn,
+                int64_t conn_capacity, int64_t* counts, void* stream);
+
+/* Per-cell marching-cubes classification (the per-cell form of
+ * 26_marching_cubes.py:435-450 classify_cells): cases[cell] = 8-corner case
+ * index, ntris[cell] = triangles of that case (0 where mask != 0).  Either
+ * output may be NULL.  Uses the fe workspace for niso = 1.  Asynchronous. */
+int tkmc_mc_classify_cells(const float* scalar, int64_t nx, int64_t ny,
+                           int64_t nz, float isovalue, const int32_t* mask,
+                           void* workspace, size_t workspace_bytes,
+                           uint8_t* cases, int32_t* ntris, void* stream);
+
+/* ---- test hooks --------------------------------------------------------- */
+
+/* Bound, in nanoseconds, on every device-side wait (decoupled look-back).
+ * Default 1e9.  Values <= 0 restore the default.  Process-wide. */
+void tkmc_set_wait_limit_ns(int64_t ns);
+
+/* Testing: make the next fe scan launch skip publishing the status of tile
+ * `tile` (-1 = off) so that its successors' bounded waits expire and the call
+ * returns TKMC_ERR_DEVICE_TIMEOUT instead of hanging.  One-shot. */
+void tkmc_test_skip_publish(int64_t tile);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TACKMC_H */

@@ -1,0 +1,284 @@
+"""Flying edges isosurface (merged-point marching cubes) on sm_100a.
+
+Drop-in for packages/tack-vis/src/tack/algorithms/flying_edges.py: the same
+``flying_edges(scalar, grid, isovalue)`` and
+``flying_edges_multiblock(blocks, isovalue)`` entry points, the same
+``UniformGrid`` descriptor and ``MCTables``, and the same result dict
+(``points``, ``conn``, ``points_field``, ``conn_field``, ``total_points``,
+``total_tris``, ``block_point_counts``, ``block_tri_counts``; ``None`` when
+the surface is empty).  Points, connectivity, counts and offsets are
+bit-identical to the reference's.
+
+Differences, all extensions:
+
+* ``isovalue`` may be a sequence: each isovalue's points and triangles
+  follow the previous one's (conn offset by the points before it), and the
+  dict adds ``isovalue_point_counts`` / ``isovalue_tri_counts``.  Up to 8
+  isovalues share one read of the volume.
+* Without a ``mask`` no zero mask is allocated (the reference allocates and
+  fills a 4 B/cell mask per call, flying_edges.py:783-788) and the block
+  dicts are not modified.
+* ``copy_to_host=False`` skips the device->host copies; ``points`` and
+  ``conn`` are then ``None`` and the fields hold the result.
+
+Each call: one ``tkmc_fe_count`` per block and group of <= 8 isovalues (one
+volume read + a single-pass scan + a 32-byte-per-isovalue host read of the
+totals), exact-size output allocation, one ``tkmc_fe_emit``.
+"""
+
+import ctypes
+from collections.abc import Sequence
+
+import numpy as np
+import torch
+
+from .. import _lib
+from ..field import Field, CUDABuffer, device_tensor, f32, field, i32
+from ..runtime import current_device, current_stream, workspace
+
+__all__ = ["UniformGrid", "MCTables", "flying_edges", "flying_edges_multiblock",
+           "_TRI_TABLE", "_NUM_TRIS", "_EDGE_CORNERS"]
+
+
+def _load_tables():
+    tri = np.zeros(4096, np.int32)
+    num = np.zeros(256, np.int32)
+    edges = np.zeros(24, np.int32)
+    _lib.check(_lib.load().tkmc_mc_tables(tri.ctypes.data, num.ctypes.data, edges.ctypes.data),
+               "tkmc_mc_tables")
+    return tri, num, edges
+
+
+_TABLE_NAMES = ("_TRI_TABLE", "_NUM_TRIS", "_EDGE_CORNERS")
+_tables = None
+
+
+def __getattr__(name):
+    """_TRI_TABLE, _NUM_TRIS, _EDGE_CORNERS: the case tables the kernels use,
+    read back from the library on first access."""
+    global _tables
+    if name in _TABLE_NAMES:
+        if _tables is None:
+            _tables = dict(zip(_TABLE_NAMES, _load_tables()))
+        return _tables[name]
+    raise AttributeError(name)
+
+
+class UniformGrid:
+    """Uniform grid descriptor: nx, ny, nz cells, origin and spacing.
+
+    Same constructor and attributes as flying_edges.py:313-341.
+    """
+
+    def __init__(self, nx, ny, nz, x0, y0, z0, dx, dy, dz):
+        self.nx = nx
+        self.ny = ny
+        self.nz = nz
+        self.nx_p1 = nx + 1
+        self.ny_p1 = ny + 1
+        self.nxy_p1 = (nx + 1) * (ny + 1)
+        self.x0 = x0
+        self.y0 = y0
+        self.z0 = z0
+        self.dx = dx
+        self.dy = dy
+        self.dz = dz
+
+    def get_x(self, i, j, k):
+        return float(np.float32(self.x0) + np.float32(i) * np.float32(self.dx))
+
+    def get_y(self, i, j, k):
+        return float(np.float32(self.y0) + np.float32(j) * np.float32(self.dy))
+
+    def get_z(self, i, j, k):
+        return float(np.float32(self.z0) + np.float32(k) * np.float32(self.dz))
+
+    @property
+    def n_nodes(self):
+        return (self.nx + 1) * (self.ny + 1) * (self.nz + 1)
+
+    @property
+    def n_cells(self):
+        return self.nx * self.ny * self.nz
+
+
+
+class MCTables:
+    """Marching-cubes lookup tables as device fields (flying_edges.py:344-357).
+
+    The kernels read their own copy from constant memory; these fields exist
+    for callers that use the tables directly.
+    """
+
+    def __init__(self):
+        tri, num, _ = _load_tables()
+        self.tri_table = field(i32, (4096,))
+        self.tri_table.from_numpy(tri)
+        self.num_tris = field(i32, (256,))
+        self.num_tris.from_numpy(num)
+
+
+def _isovalue_list(isovalue):
+    if isinstance(isovalue, (str, bytes)):
+        raise TypeError("isovalue must be a number or a sequence of numbers")
+    if isinstance(isovalue, (Sequence, np.ndarray, torch.Tensor)):
+        vals = [float(v) for v in (isovalue.tolist() if hasattr(isovalue, "tolist") else isovalue)]
+        if not vals:
+            raise ValueError("empty list of isovalues")
+        return vals, True
+    return [float(isovalue)], False
+
+
+def _geom6(g):
+    """{x0, y0, z0, dx, dy, dz} of any grid with UniformGrid's attributes."""
+    return (ctypes.c_float * 6)(g.x0, g.y0, g.z0, g.dx, g.dy, g.dz)
+
+
+def _f32_array(vals):
+    return (ctypes.c_float * len(vals))(*vals)
+
+
+def _i64_array(vals):
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+class _Block:
+    def __init__(self, blk, idx):
+        if "scalar" not in blk or "grid" not in blk:
+            raise KeyError(f"block {idx} needs 'scalar' and 'grid'")
+        self.grid = blk["grid"]
+        g = self.grid
+        if min(g.nx, g.ny, g.nz) < 0:
+            raise ValueError(f"block {idx}: negative grid size")
+        self.scalar = device_tensor(blk["scalar"], f32)
+        n_nodes = (g.nx + 1) * (g.ny + 1) * (g.nz + 1)
+        if self.scalar.numel() != n_nodes:
+            raise ValueError(f"block {idx}: field has {self.scalar.numel()} values, grid needs "
+                             f"{n_nodes}")
+        m = blk.get("mask")
+        self.mask = None if m is None else device_tensor(m, i32)
+        if self.mask is not None and self.mask.numel() != g.nx * g.ny * g.nz:
+            raise ValueError(f"block {idx}: mask has {self.mask.numel()} values, grid has "
+                             f"{g.nx * g.ny * g.nz} cells")
+        self.counts = []  # per isovalue group: (host int64 [niso*4], workspace)
+
+
+def flying_edges(scalar, grid, isovalue, *, copy_to_host=True):
+    """Isosurface a single uniform grid block.
+
+    Args:
+        scalar: f32 field of node values, (nx+1)*(ny+1)*(nz+1) values with i
+            fastest (a tack_b200 Field, a torch CUDA tensor, a reference tack
+            field on its CUDA backend, or a numpy array).
+        grid: UniformGrid.
+        isovalue: threshold, or a sequence of thresholds.
+
+    Returns:
+        dict with 'points' (numpy f32 (n,3)), 'conn' (numpy i32 (m,3)),
+        'points_field', 'conn_field', 'total_points', 'total_tris', ...;
+        None if empty.
+    """
+    return flying_edges_multiblock([{"scalar": scalar, "grid": grid}], isovalue,
+                                   copy_to_host=copy_to_host)
+
+
+def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
+    """Isosurface a list of uniform grid blocks into one output.
+
+    Args:
+        blocks: list of dicts with 'scalar' and 'grid', optionally 'mask'
+            (int32 per cell; nonzero cells emit no triangles).
+        isovalue: threshold, or a sequence of thresholds.
+
+    Returns:
+        dict as flying_edges(); blocks (and isovalues) are concatenated in
+        order, each block's conn offset by the points before it.  None if
+        there are no points or no triangles.
+    """
+    if len(blocks) == 0:
+        return None
+    isos, is_list = _isovalue_list(isovalue)
+    lib = _lib.load()
+    dev = current_device()
+    stream = current_stream(dev)
+    bl = [_Block(b, i) for i, b in enumerate(blocks)]
+    groups = [isos[i:i + _lib.MAX_ISO] for i in range(0, len(isos), _lib.MAX_ISO)]
+
+    # Pass 1: count every (block, isovalue group).  Emit needs each part's
+    # offsets, so a call with several parts gives each its own workspace;
+    # a single part reuses this thread's cached one.
+    private = len(bl) * len(groups) > 1
+    for b in bl:
+        g = b.grid
+        for grp in groups:
+            nbytes = lib.tkmc_fe_workspace_bytes(g.nx, g.ny, g.nz, len(grp))
+            if nbytes == 0:
+                raise ValueError(f"unsupported grid {g.nx} x {g.ny} x {g.nz}")
+            ws = (torch.empty(nbytes, dtype=torch.uint8, device=dev) if private
+                  else workspace("fe", nbytes, dev))
+            counts = np.zeros(4 * len(grp), np.int64)
+            _lib.check(lib.tkmc_fe_count(
+                b.scalar.data_ptr(), g.nx, g.ny, g.nz, 0, _f32_array(grp), len(grp),
+                b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(), ws.numel(),
+                counts.ctypes.data, stream), "tkmc_fe_count")
+            b.counts.append((counts, ws))
+
+    # Layout: isovalue-major, then block, then the X | Y | Z sections.
+    niso, nblk = len(isos), len(bl)
+    pts = np.zeros((niso, nblk, 3), np.int64)
+    tris = np.zeros((niso, nblk), np.int64)
+    for bi, b in enumerate(bl):
+        for gi, (counts, _) in enumerate(b.counts):
+            for q in range(len(groups[gi])):
+                qi = gi * _lib.MAX_ISO + q
+                pts[qi, bi] = counts[4 * q:4 * q + 3]
+                tris[qi, bi] = counts[4 * q + 3]
+    block_pts = pts.sum(axis=2)  # [iso, block]
+    total_points = int(block_pts.sum())
+    total_tris = int(tris.sum())
+    if total_points == 0 or total_tris == 0:
+        return None
+    if total_points > 0x7FFFFFFF:
+        raise OverflowError(f"{total_points} points do not fit int32 point ids")
+    start_pt = np.concatenate([[0], np.cumsum(block_pts.reshape(-1))[:-1]]).reshape(niso, nblk)
+    start_tri = np.concatenate([[0], np.cumsum(tris.reshape(-1))[:-1]]).reshape(niso, nblk)
+
+    points_t = torch.empty(total_points * 3, dtype=torch.float32, device=dev)
+    conn_t = torch.empty(total_tris * 3, dtype=torch.int32, device=dev)
+
+    # Pass 2: emit.
+    for bi, b in enumerate(bl):
+        g = b.grid
+        for gi, grp in enumerate(groups):
+            _, ws = b.counts[gi]
+            ids, tri_base = [], []
+            for q in range(len(grp)):
+                qi = gi * _lib.MAX_ISO + q
+                p0 = start_pt[qi, bi]
+                X, Y = pts[qi, bi, 0], pts[qi, bi, 1]
+                ids += [p0, p0 + X, p0 + X + Y]
+                tri_base.append(start_tri[qi, bi])
+            ida = _i64_array(ids)
+            _lib.check(lib.tkmc_fe_emit(
+                b.scalar.data_ptr(), g.nx, g.ny, g.nz, 0, 0, _geom6(g), _f32_array(grp),
+                len(grp), b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(),
+                ws.numel(), ida, ida, _i64_array(tri_base), points_t.data_ptr(),
+                conn_t.data_ptr(), stream), "tkmc_fe_emit")
+
+    points_field = Field(f32, (total_points * 3,), CUDABuffer(points_t))
+    conn_field = Field(i32, (total_tris * 3,), CUDABuffer(conn_t))
+    out = {
+        "points": points_t.cpu().numpy().reshape(-1, 3) if copy_to_host else None,
+        "conn": conn_t.cpu().numpy().reshape(-1, 3) if copy_to_host else None,
+        "points_field": points_field,
+        "conn_field": conn_field,
+        "total_points": total_points,
+        "total_tris": total_tris,
+        "block_point_counts": [int(x) for x in block_pts.sum(axis=0)],
+        "block_tri_counts": [int(x) for x in tris.sum(axis=0)],
+    }
+    if is_list:
+        out["isovalues"] = list(isos)
+        out["isovalue_point_counts"] = [int(x) for x in block_pts.sum(axis=1)]
+        out["isovalue_tri_counts"] = [int(x) for x in tris.sum(axis=1)]
+    return out

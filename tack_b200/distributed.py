@@ -1,0 +1,198 @@
+"""Z-slab sharded flying edges: one process per GPU on one node.
+
+The volume is split into contiguous runs of node planes.  Rank r owns node
+planes [p0, p1) and also holds plane p1 as a read-only ghost (except the last
+rank), so it can close its last layer of cells.  Each rank classifies,
+counts and scans its slab independently (tkmc_fe_count with ghost_plane=1);
+the only exchange is ONE all-gather of 4 int64 totals per isovalue per rank
+(NCCL over NVLink).  From the gathered totals every rank computes the global
+point-id bases of its x, y and z sections, then emits its points and
+triangles into rank-local buffers holding exactly its slices of the global
+output.  Point ids in conn are global, and the assembled output is
+byte-identical to a single-volume flying_edges call: seams are merged, not
+duplicated (unlike flying_edges_multiblock, flying_edges.py:766-832, whose
+blocks mesh independently).
+
+Ghost-plane x/y edges belong to the next rank.  This rank's scan also covers
+the ghost rows, after its own rows, so their offsets continue from this
+rank's own totals -- which is exactly where the next rank's sections start.
+"""
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib
+from .field import CUDABuffer, Field, f32, i32
+from .runtime import current_device, current_stream
+
+
+class SlabPlan:
+    """Node-plane ownership of `rank` among `world` for nz_nodes planes."""
+
+    def __init__(self, nz_nodes, world, rank):
+        if not (0 <= rank < world) or nz_nodes < 2 * world:
+            raise ValueError(f"cannot split {nz_nodes} planes over {world} ranks")
+        base, rem = divmod(nz_nodes, world)
+        self.rank, self.world, self.nz_nodes = rank, world, nz_nodes
+        self.p0 = rank * base + min(rank, rem)
+        self.p1 = self.p0 + base + (1 if rank < rem else 0)
+        self.ghost = self.p1 < nz_nodes
+        self.k0 = self.p0                      # first local plane
+        self.k1 = min(self.p1 + 1, nz_nodes)   # one past the last local plane
+        self.nz_cells = self.k1 - self.k0 - 1  # cell layers in the local grid
+
+    @property
+    def local_planes(self):
+        return self.k1 - self.k0
+
+    def __repr__(self):
+        return (f"SlabPlan(rank={self.rank}/{self.world}, own=[{self.p0},{self.p1}), "
+                f"local=[{self.k0},{self.k1}), ghost={self.ghost})")
+
+
+def slab_bases(all_counts, rank):
+    """Offsets of `rank`'s output within the global layout.
+
+    all_counts: int64 [world, niso, 4] = per rank and isovalue {X, Y, Z, T}.
+    Global layout is isovalue-major; within an isovalue the x section of
+    every rank (in rank order), then all y, then all z -- the single-volume
+    layout.  Returns dict of int64 arrays:
+      id_base  [niso, 3]  global id of this rank's first x / y / z point
+      out_base [niso, 3]  rank-local row of this rank's first x / y / z point
+      tri_out  [niso]     rank-local row of this rank's first triangle
+      tri_global [niso]   global row of this rank's first triangle
+      pt_global_out [niso, 3] global row of the first x/y/z point (== id_base)
+      totals   [niso, 2]  global points and triangles per isovalue
+    """
+    c = np.asarray(all_counts, np.int64)
+    world, niso, _ = c.shape
+    tot = c.sum(axis=0)                      # [niso, 4]
+    P = tot[:, :3].sum(axis=1)               # global points per isovalue
+    Pq = np.concatenate([[0], np.cumsum(P)[:-1]])
+    Tq = np.concatenate([[0], np.cumsum(tot[:, 3])[:-1]])
+    before = c[:rank].sum(axis=0)            # [niso, 4] earlier ranks
+    id_base = np.stack([Pq + before[:, 0],
+                        Pq + tot[:, 0] + before[:, 1],
+                        Pq + tot[:, 0] + tot[:, 1] + before[:, 2]], axis=1)
+    own = c[rank]
+    own_p = own[:, :3].sum(axis=1)
+    lp = np.concatenate([[0], np.cumsum(own_p)[:-1]])
+    out_base = np.stack([lp, lp + own[:, 0], lp + own[:, 0] + own[:, 1]], axis=1)
+    tri_out = np.concatenate([[0], np.cumsum(own[:, 3])[:-1]])
+    return {"id_base": id_base, "out_base": out_base, "tri_out": tri_out,
+            "tri_global": Tq + before[:, 3], "pt_global_out": id_base,
+            "totals": np.stack([P, tot[:, 3]], axis=1)}
+
+
+def _i64(vals):
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in np.asarray(vals).reshape(-1)])
+
+
+def _f32(vals):
+    return (ctypes.c_float * len(vals))(*[float(v) for v in vals])
+
+
+class SlabEngine:
+    """Per-rank state: plan, workspace and the collective used for totals."""
+
+    def __init__(self, grid, plan, isovalues, group=None):
+        if len(isovalues) > _lib.MAX_ISO:
+            raise ValueError(f"at most {_lib.MAX_ISO} isovalues per slab call")
+        self.grid, self.plan, self.isos = grid, plan, list(isovalues)
+        self.group = group
+        self.dev = current_device()
+        self.lib = _lib.load()
+        nx, ny = grid.nx, grid.ny
+        self.nbytes = self.lib.tkmc_fe_workspace_bytes(nx, ny, plan.nz_cells, len(self.isos))
+        self.ws = torch.empty(self.nbytes, dtype=torch.uint8, device=self.dev)
+        self.counts_dev = torch.zeros(len(self.isos) * 4, dtype=torch.int64, device=self.dev)
+        world = plan.world
+        self.gathered = torch.zeros(world * len(self.isos) * 4, dtype=torch.int64,
+                                    device=self.dev)
+
+    def count(self, local_values):
+        g, p, lib = self.grid, self.plan, self.lib
+        niso = len(self.isos)
+        counts = np.zeros(niso * 4, np.int64)
+        _lib.check(lib.tkmc_fe_count(local_values.data_ptr(), g.nx, g.ny, p.nz_cells,
+                                     1 if p.ghost else 0, _f32(self.isos), niso, None,
+                                     self.ws.data_ptr(), self.nbytes, counts.ctypes.data,
+                                     current_stream(self.dev)), "tkmc_fe_count")
+        return counts.reshape(niso, 4)
+
+    def exchange(self, counts):
+        """All-gather every rank's totals (one collective)."""
+        import torch.distributed as dist
+        niso = len(self.isos)
+        if self.plan.world == 1:
+            return counts.reshape(1, niso, 4)
+        self.counts_dev.copy_(torch.from_numpy(counts.reshape(-1)))
+        dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
+        return self.gathered.cpu().numpy().reshape(self.plan.world, niso, 4)
+
+    def emit(self, local_values, counts, bases):
+        g, p, lib = self.grid, self.plan, self.lib
+        own_p = int(counts[:, :3].sum())
+        own_t = int(counts[:, 3].sum())
+        pts = torch.empty(max(own_p, 1) * 3, dtype=torch.float32, device=self.dev)
+        conn = torch.empty(max(own_t, 1) * 3, dtype=torch.int32, device=self.dev)
+        if own_p or own_t:
+            _lib.check(lib.tkmc_fe_emit(
+                local_values.data_ptr(), g.nx, g.ny, p.nz_cells, 1 if p.ghost else 0, p.k0,
+                _f32([g.x0, g.y0, g.z0, g.dx, g.dy, g.dz]), _f32(self.isos), len(self.isos),
+                None, self.ws.data_ptr(), self.nbytes, _i64(bases["id_base"]),
+                _i64(bases["out_base"]), _i64(bases["tri_out"]), pts.data_ptr(),
+                conn.data_ptr(), current_stream(self.dev)), "tkmc_fe_emit")
+        return pts[:own_p * 3], conn[:own_t * 3]
+
+    def run(self, local_values):
+        """count -> all-gather totals -> emit.  Returns this rank's slices."""
+        counts = self.count(local_values)
+        allc = self.exchange(counts)
+        if allc.max() > np.iinfo(np.int32).max or \
+                int(allc[:, :, :3].sum()) > np.iinfo(np.int32).max:
+            raise OverflowError("global point total does not fit int32 point ids")
+        b = slab_bases(allc, self.plan.rank)
+        pts, conn = self.emit(local_values, counts, b)
+        return {"points_field": Field(f32, (pts.numel(),), CUDABuffer(pts)),
+                "conn_field": Field(i32, (conn.numel(),), CUDABuffer(conn)),
+                "counts": counts, "all_counts": allc, "bases": b,
+                "total_points": int(b["totals"][:, 0].sum()),
+                "total_tris": int(b["totals"][:, 1].sum())}
+
+
+def flying_edges_zslab(local_values, grid, plan, isovalues, group=None):
+    """Sharded isosurface of one rank's slab; see module docstring.
+
+    local_values: f32 CUDA tensor of planes [plan.k0, plan.k1) of the whole
+    volume (grid = the whole volume's UniformGrid).
+    """
+    return SlabEngine(grid, plan, isovalues, group).run(local_values)
+
+
+def assemble(parts):
+    """Host-side assembly of every rank's result into the single-volume
+    output (points (P,3), conn (T,3)).  parts: per rank a dict with numpy
+    'points' (flat), 'conn' (flat), 'counts' [niso,4] and 'bases'."""
+    b0 = parts[0]["bases"]
+    P = int(b0["totals"][:, 0].sum())
+    T = int(b0["totals"][:, 1].sum())
+    points = np.empty((P, 3), np.float32)
+    conn = np.empty((T, 3), np.int32)
+    for part in parts:
+        c, b = part["counts"], part["bases"]
+        pts = np.asarray(part["points"]).reshape(-1, 3)
+        cn = np.asarray(part["conn"]).reshape(-1, 3)
+        for q in range(c.shape[0]):
+            for s in range(3):
+                n = int(c[q, s])
+                lo = int(b["out_base"][q, s])
+                go = int(b["pt_global_out"][q, s])
+                points[go:go + n] = pts[lo:lo + n]
+            n = int(c[q, 3])
+            lo = int(b["tri_out"][q])
+            go = int(b["tri_global"][q])
+            conn[go:go + n] = cn[lo:lo + n]
+    return points, conn

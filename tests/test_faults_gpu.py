@@ -1,0 +1,64 @@
+"""Bounded device-side waits end in an error status, never a hang.
+
+The decoupled look-back spins on predecessor tiles' status flags.  A test
+hook makes one tile skip publishing its status, so its successors' waits can
+only end by the time limit (set short here); the call must return
+TKMC_ERR_DEVICE_TIMEOUT, and the context must stay usable.  Nothing faults,
+traps or hangs the GPU.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_fe_case
+from fe_helpers import capi_fe, f32arr, stream
+from tack_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture
+def short_wait():
+    lib = _lib.load()
+    lib.tkmc_set_wait_limit_ns(20_000_000)  # 20 ms
+    yield lib
+    lib.tkmc_set_wait_limit_ns(0)
+    lib.tkmc_test_skip_publish(-1)
+
+
+def test_fe_scan_wait_expires_with_status(tack, short_wait):
+    lib = short_wait
+    c = load_fe_case("gyroid48")  # 48*48 node rows -> 9 tiles
+    nx, ny, nz = c["grid_tuple"][:3]
+    v = torch.from_numpy(c["values"]).cuda()
+    nb = lib.tkmc_fe_workspace_bytes(nx, ny, nz, 1)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    counts = np.zeros(4, np.int64)
+    lib.tkmc_test_skip_publish(3)
+    rc = lib.tkmc_fe_count(v.data_ptr(), nx, ny, nz, 0, f32arr([0.0]), 1, None, ws.data_ptr(), nb,
+                           counts.ctypes.data, stream())
+    assert rc == _lib.TKMC_ERR_DEVICE_TIMEOUT
+    assert b"wait expired" in lib.tkmc_last_error()
+    # The context is intact: the next call succeeds and matches the reference.
+    got = capi_fe(c["values"], c["grid_tuple"], [0.0])
+    np.testing.assert_array_equal(got["conn"], c["conn"])
+
+
+def test_scan_wait_expires_with_status(tack, short_wait):
+    lib = short_wait
+    n = 5 * 4096 + 17
+    a = torch.ones(n, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(a)
+    nb = lib.tkmc_scan_workspace_bytes(n)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    import ctypes
+    tot = ctypes.c_int64(0)
+    lib.tkmc_test_skip_publish(2)
+    rc = lib.tkmc_scan_i32(a.data_ptr(), out.data_ptr(), n, 0, ws.data_ptr(), nb,
+                           ctypes.byref(tot), stream())
+    assert rc == _lib.TKMC_ERR_DEVICE_TIMEOUT
+    rc = lib.tkmc_scan_i32(a.data_ptr(), out.data_ptr(), n, 0, ws.data_ptr(), nb,
+                           ctypes.byref(tot), stream())
+    assert rc == 0 and tot.value == n
+    assert torch.equal(out.cpu(), torch.arange(n, dtype=torch.int32))

@@ -1,0 +1,197 @@
+"""Flying edges on the GPU against the reference's own outputs.
+
+Every golden fixture was produced by the reference (tack.cpu).  The GPU
+result must be identical: totals, per-row offsets (scan), connectivity, and
+point coordinates bit for bit (the kernels use the reference's f32
+operation order without contraction; the tolerance the north star allows,
+1e-5 relative, is not needed).
+"""
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, golden_fe_cases, load_fe_case
+from fe_helpers import assert_same_surface, capi_fe, reference_offsets_from_rows
+
+pytestmark = pytest.mark.gpu
+
+
+def _upload(tack, arr, dtype):
+    f = tack.field(dtype, (arr.size,))
+    f.from_numpy(arr)
+    return f
+
+
+@pytest.mark.parametrize("name", golden_fe_cases())
+def test_api_matches_reference(tack, name):
+    """tack_b200.flying_edges_multiblock == the reference's output."""
+    c = load_fe_case(name)
+    grid = tack.UniformGrid(*c["grid_tuple"])
+    blk = {"scalar": _upload(tack, c["values"], tack.f32), "grid": grid}
+    if c["mask"] is not None:
+        blk["mask"] = _upload(tack, c["mask"], tack.i32)
+    r = tack.flying_edges_multiblock([blk], c["isovalue"])
+    if int(c["is_none"]):
+        assert r is None
+        return
+    ref = {"total_points": int(c["totals"][0]), "total_tris": int(c["totals"][1]),
+           "points": c["points"], "conn": c["conn"]}
+    assert_same_surface(r, ref)
+    assert r["block_point_counts"] == [ref["total_points"]]
+    assert r["block_tri_counts"] == [ref["total_tris"]]
+    np.testing.assert_array_equal(r["points_field"].to_numpy().reshape(-1, 3), r["points"])
+    np.testing.assert_array_equal(r["conn_field"].to_numpy().reshape(-1, 3), r["conn"])
+
+
+@pytest.mark.parametrize("name", golden_fe_cases())
+def test_capi_counts_and_offsets_match_reference(tack, name):
+    """Through the raw C ABI: the scan offsets equal _count_block's."""
+    c = load_fe_case(name)
+    g = c["grid_tuple"]
+    got = capi_fe(c["values"], g, [c["isovalue"]], c["mask"], want_rows=True)
+    xo, yo, zo, to = reference_offsets_from_rows(got["rows"][0], got["counts"][0], g)
+    np.testing.assert_array_equal(xo, c["xo"])
+    np.testing.assert_array_equal(yo, c["yo"])
+    np.testing.assert_array_equal(zo, c["zo"])
+    np.testing.assert_array_equal(to, c["tri_offsets"])
+    assert int(got["counts"][0, :3].sum()) == int(c["count_totals"][0])
+    assert int(got["counts"][0, 3]) == int(c["count_totals"][1])
+    if not int(c["is_none"]):
+        ref = {"total_points": int(c["totals"][0]), "total_tris": int(c["totals"][1]),
+               "points": c["points"], "conn": c["conn"]}
+        assert_same_surface(got, ref)
+
+
+def test_multiblock_matches_reference(tack):
+    z = np.load(f"{GOLDEN}/fe_multiblock_sphere24.npz")
+    blocks = []
+    for b in (0, 1):
+        g = z[f"grid{b}"]
+        grid = tack.UniformGrid(int(g[0]), int(g[1]), int(g[2]), *g[3:])
+        blocks.append({"scalar": _upload(tack, z[f"values{b}"], tack.f32), "grid": grid})
+    r = tack.flying_edges_multiblock(blocks, 0.0)
+    np.testing.assert_array_equal(r["conn"], z["conn"])
+    np.testing.assert_array_equal(r["points"].view(np.uint32), z["points"].view(np.uint32))
+    assert r["block_point_counts"] == list(z["block_point_counts"])
+    assert r["block_tri_counts"] == list(z["block_tri_counts"])
+
+
+def test_isovalue_list_matches_per_isovalue_reference(tack, oracle):
+    """A list of isovalues == the oracle's per-isovalue calls, concatenated."""
+    c = load_fe_case("gyroid48")
+    g = c["grid_tuple"]
+    isos = [-0.5, -0.1, 0.0, 0.3, 0.7, 1.2, -1.0, 0.05, 0.5]  # 9: two groups
+    f = _upload(tack, c["values"], tack.f32)
+    r = tack.flying_edges(f, tack.UniformGrid(*g), isos)
+    ref = oracle.flying_edges_isovalues(c["values"], oracle.Grid(*g), isos)
+    assert_same_surface(r, ref)
+    assert r["isovalue_point_counts"] == ref["isovalue_point_counts"]
+    assert r["isovalue_tri_counts"] == ref["isovalue_tri_counts"]
+
+
+def test_capi_multi_isovalue_one_read(tack, oracle):
+    """tkmc_fe_count with 8 isovalues classifies all of them in one launch."""
+    c = load_fe_case("blobs72")
+    g = c["grid_tuple"]
+    isos = [0.05, 0.1, 0.2, 0.3, 0.5, 0.7, 0.9, 1.1]
+    got = capi_fe(c["values"], g, isos, want_rows=True)
+    ref = oracle.flying_edges_isovalues(c["values"], oracle.Grid(*g), isos)
+    assert_same_surface(got, ref)
+    for q, iso in enumerate(isos):
+        info = oracle.count_block(c["values"], oracle.Grid(*g), iso)
+        xo, yo, zo, to = reference_offsets_from_rows(got["rows"][q], got["counts"][q], g)
+        np.testing.assert_array_equal(xo, info["xo"])
+        np.testing.assert_array_equal(yo, info["yo"])
+        np.testing.assert_array_equal(zo, info["zo"])
+        np.testing.assert_array_equal(to, info["tri_offsets"])
+
+
+def test_fe_run_capacity_protocol(tack):
+    """tkmc_fe_run: too-small buffers -> TKMC_ERR_CAPACITY with counts."""
+    import ctypes
+
+    import torch
+
+    from fe_helpers import f32arr, stream
+    from tack_b200 import _lib
+    c = load_fe_case("c1_sphere64")
+    nx, ny, nz = c["grid_tuple"][:3]
+    lib = _lib.load()
+    v = torch.from_numpy(c["values"]).cuda()
+    nb = lib.tkmc_fe_workspace_bytes(nx, ny, nz, 1)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    counts = np.zeros(4, np.int64)
+    pts = torch.empty(3 * 100, dtype=torch.float32, device="cuda")
+    conn = torch.empty(3 * 100, dtype=torch.int32, device="cuda")
+    rc = lib.tkmc_fe_run(v.data_ptr(), nx, ny, nz, f32arr(c["grid_tuple"][3:]), f32arr([0.0]), 1,
+                         None, ws.data_ptr(), nb, pts.data_ptr(), 100, conn.data_ptr(), 100,
+                         counts.ctypes.data, stream())
+    assert rc == _lib.TKMC_ERR_CAPACITY
+    assert int(counts[:3].sum()) == 7584 and int(counts[3]) == 15164
+    P, T = int(counts[:3].sum()), int(counts[3])
+    pts = torch.empty(3 * P, dtype=torch.float32, device="cuda")
+    conn = torch.empty(3 * T, dtype=torch.int32, device="cuda")
+    rc = lib.tkmc_fe_run(v.data_ptr(), nx, ny, nz, f32arr(c["grid_tuple"][3:]), f32arr([0.0]), 1,
+                         None, ws.data_ptr(), nb, pts.data_ptr(), P, conn.data_ptr(), T,
+                         counts.ctypes.data, stream())
+    assert rc == 0
+    np.testing.assert_array_equal(conn.cpu().numpy().reshape(-1, 3), c["conn"])
+    np.testing.assert_array_equal(pts.cpu().numpy().reshape(-1, 3).view(np.uint32),
+                                  c["points"].view(np.uint32))
+    del ctypes
+
+
+def test_unaligned_volume_pointer(tack, oracle):
+    """A volume that does not start on a 16-byte boundary (scalar loads)."""
+    import torch
+    c = load_fe_case("noise_19x13x11")
+    g = c["grid_tuple"]
+    buf = torch.empty(c["values"].size + 1, dtype=torch.float32, device="cuda")
+    buf[1:] = torch.from_numpy(c["values"]).cuda()
+    got = capi_fe(buf[1:], g, [c["isovalue"]])
+    ref = {"total_points": int(c["totals"][0]), "total_tris": int(c["totals"][1]),
+           "points": c["points"], "conn": c["conn"]}
+    assert_same_surface(got, ref)
+
+
+def test_reference_cuda_field_duck_typing(tack):
+    """A field exposing only ._buffer.device_ptr and .shape (as tack.cuda's
+    fields do) is accepted without a copy."""
+    c = load_fe_case("sphere24_in")
+    f = _upload(tack, c["values"], tack.f32)
+
+    class Buf:
+        device_ptr = f._buffer.device_ptr
+
+    class RefField:
+        _buffer = Buf()
+        shape = f.shape
+
+    r = tack.flying_edges(RefField(), tack.UniformGrid(*c["grid_tuple"]), 0.0)
+    np.testing.assert_array_equal(r["conn"], c["conn"])
+
+
+def test_empty_and_uniform_volumes(tack):
+    g = tack.UniformGrid(7, 5, 3, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+    n = 8 * 6 * 4
+    for val in (-1.0, 1.0, 0.0):
+        f = _upload(tack, np.full(n, val, np.float32), tack.f32)
+        assert tack.flying_edges(f, g, 0.0) is None
+    f = _upload(tack, np.full(n, np.nan, np.float32), tack.f32)
+    assert tack.flying_edges(f, g, 0.0) is None
+    assert tack.flying_edges_multiblock([], 0.0) is None
+
+
+def test_degenerate_grids_match_oracle(tack, oracle):
+    """Grids with one or zero cells along an axis."""
+    rng = np.random.default_rng(5)
+    for shape in ((0, 4, 4), (4, 0, 4), (4, 4, 0), (1, 1, 1), (0, 0, 3), (33, 1, 0), (1, 40, 2)):
+        nx, ny, nz = shape
+        v = rng.standard_normal((nx + 1) * (ny + 1) * (nz + 1)).astype(np.float32)
+        g = (nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+        got = tack.flying_edges(_upload(tack, v, tack.f32), tack.UniformGrid(*g), 0.0)
+        ref = oracle.flying_edges(v, oracle.Grid(*g), 0.0)
+        if ref is None:
+            assert got is None
+        else:
+            assert_same_surface(got, ref)

@@ -1,0 +1,118 @@
+"""Scan, field reductions and per-cell classification on the GPU.
+
+Known answers come from the reference's own tests and fixtures
+(tests/golden/scan.npz, reduce.npz, mc_classify.npz); larger cases are
+checked against the oracle.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def _field(tack, arr, dtype):
+    f = tack.field(dtype, (arr.size,))
+    f.from_numpy(arr)
+    return f
+
+
+def test_scan_known_answers(tack):
+    z = np.load(f"{GOLDEN}/scan.npz")
+    keys = sorted({k.rsplit("_", 1)[0] for k in z.files if k.endswith("_in")})
+    for k in keys:
+        a = z[f"{k}_in"]
+        inp, out = _field(tack, a, tack.i32), tack.field(tack.i32, (a.size,))
+        tot = tack.algorithms.exclusive_scan(inp, out, a.size)
+        np.testing.assert_array_equal(out.to_numpy(), z[f"{k}_excl"])
+        assert tot == int(z[f"{k}_excl_total"])
+        tot = tack.algorithms.inclusive_scan(inp, out, a.size)
+        np.testing.assert_array_equal(out.to_numpy(), z[f"{k}_incl"])
+        assert tot == int(z[f"{k}_incl_total"])
+        np.testing.assert_array_equal(inp.to_numpy(), a)  # input preserved
+
+
+@pytest.mark.parametrize("n", [1, 31, 4095, 4096, 4097, 1 << 20, 3_000_017])
+def test_scan_sizes_match_oracle(tack, oracle, n):
+    a = np.random.default_rng(n).integers(-50, 1000, n).astype(np.int32)
+    inp, out = _field(tack, a, tack.i32), tack.field(tack.i32, (n,))
+    tot = tack.algorithms.exclusive_scan(inp, out, n)
+    ref, rtot = oracle.scan(a)
+    np.testing.assert_array_equal(out.to_numpy(), ref)
+    assert tot == rtot
+
+
+def test_scan_wraps_like_int32_and_aliases(tack, oracle):
+    a = np.full(50_000, 2_000_000_000 // 7, np.int32)
+    f = _field(tack, a, tack.i32)
+    tot = tack.algorithms.inclusive_scan(f, f, a.size)  # in place
+    ref, rtot = oracle.scan(a, inclusive=True)
+    np.testing.assert_array_equal(f.to_numpy(), ref)
+    assert tot == rtot == int(a.astype(np.int64).sum())
+
+
+def test_reductions_contract(tack):
+    """test_backend_contract.py:102-118: 0..7 -> 28 / 0 / 7."""
+    f = _field(tack, np.arange(8, dtype=np.float32), tack.f32)
+    assert f.sum() == pytest.approx(28.0)
+    assert f.min() == 0.0 and f.max() == 7.0
+    assert f.mean() == pytest.approx(3.5)
+
+
+def test_reductions_match_reference_fixtures(tack):
+    z = np.load(f"{GOLDEN}/reduce.npz")
+    for k in ("arange8", "rand10001", "sphere64"):
+        f = _field(tack, z[f"{k}_in"], tack.f32)
+        ref = z[f"{k}_out"]
+        assert f.min() == ref[0] and f.max() == ref[1]
+        assert f.sum() == pytest.approx(ref[2], rel=1e-5, abs=1e-3)
+
+
+@pytest.mark.parametrize("offset", [0, 1, 2, 3])
+def test_reductions_large_unaligned_with_nan(tack, oracle, offset):
+    n = 5_000_003
+    a = np.random.default_rng(9).standard_normal(n + offset).astype(np.float32)
+    a[offset + 12345] = np.nan
+    a[offset + 777] = 9.5
+    a[-1] = -11.25
+    t = torch.from_numpy(a).cuda()[offset:]
+    mn, mx, sm, nan = tack.reduce_f32(t)
+    rmn, rmx, rsm, rnan = oracle.reduce(a[offset:])
+    assert (mn, mx, nan) == (rmn, rmx, rnan) == (-11.25, 9.5, 1)
+    assert np.isnan(sm) and np.isnan(rsm)
+
+
+def test_reduction_sum_accuracy(tack):
+    a = np.random.default_rng(3).random(10_000_000).astype(np.float32)
+    f = _field(tack, a, tack.f32)
+    assert f.sum() == pytest.approx(float(a.astype(np.float64).sum()), rel=1e-12)
+
+
+def test_classify_cells_matches_reference(tack):
+    """Per-cell counts of examples/26_marching_cubes.py classify_cells and
+    their exclusive_scan offsets."""
+    z = np.load(f"{GOLDEN}/mc_classify.npz")
+    for name in ("c1", "noise"):
+        g = z[f"{name}_grid"]
+        grid = tack.UniformGrid(int(g[0]), int(g[1]), int(g[2]), *g[3:])
+        f = _field(tack, z[f"{name}_values"], tack.f32)
+        cases, ntri = tack.algorithms.classify_cells(f, grid, float(z[f"{name}_iso"]))
+        np.testing.assert_array_equal(ntri.to_numpy(), z[f"{name}_num_tri"])
+        off = tack.field(tack.i32, ntri.shape)
+        tot = tack.algorithms.exclusive_scan(ntri, off, ntri.size)
+        np.testing.assert_array_equal(off.to_numpy(), z[f"{name}_offsets"])
+        assert tot == int(z[f"{name}_total"])
+
+
+def test_classify_cases_match_oracle(tack, oracle):
+    from conftest import load_fe_case
+    c = load_fe_case("noise_95x6x3")
+    g = c["grid_tuple"]
+    f = _field(tack, c["values"], tack.f32)
+    cases, ntri = tack.algorithms.classify_cells(f, tack.UniformGrid(*g), c["isovalue"])
+    rc, rn = oracle.classify_cells(c["values"], oracle.Grid(*g), c["isovalue"])
+    np.testing.assert_array_equal(cases.to_numpy(), rc)
+    np.testing.assert_array_equal(ntri.to_numpy(), rn)
