@@ -316,6 +316,7 @@ def main():
     t_end.record(stream)
     torch.cuda.synchronize()
     launches = lib.tkmc_launch_count() - launches0
+    eng.check()  # any device-recorded error invalidates the run
     clk = clocks.stop()
     barrier()
     ms = t_start.elapsed_time(t_end)

@@ -133,7 +133,9 @@ int tkmc_fe_count(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
  * points of earlier isovalues, tri_out_base = earlier triangles.  geom6 =
  * {x0, y0, z0, dx, dy, dz}; k_offset is the global index of this slab's node
  * plane 0 (point z uses float(k + k_offset), exactly as the reference).
- * Asynchronous on `stream`.
+ * points_capacity / conn_capacity are the rows (of 3) the buffers hold; a
+ * write beyond them is skipped and recorded, and tkmc_fe_check then returns
+ * TKMC_ERR_CAPACITY.  Asynchronous on `stream`.
  * Replaces: flying_edges.py:718-746 (_emit_block: _fe_emit_points_xyz,
  * _fe_emit_tris). */
 int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
@@ -141,8 +143,15 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
                  const float* isovalues, int niso, const int32_t* mask,
                  void* workspace, size_t workspace_bytes,
                  const int64_t* pt_id_base, const int64_t* pt_out_base,
-                 const int64_t* tri_out_base, float* points, int32_t* conn,
+                 const int64_t* tri_out_base, float* points,
+                 int64_t points_capacity, int32_t* conn, int64_t conn_capacity,
                  void* stream);
+
+/* Synchronise `stream` and report any error the device recorded in the
+ * workspace during the last count/emit (TKMC_ERR_DEVICE_TIMEOUT,
+ * TKMC_ERR_CAPACITY), else TKMC_OK. */
+int tkmc_fe_check(int64_t nx, int64_t ny, int64_t nz, int niso,
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* Phase entry points of tkmc_fe_count, for callers that time or overlap the
  * phases.  classify = one volume read -> node bitmasks (asynchronous);

@@ -39,7 +39,8 @@ SIGNATURES = {
     "tkmc_fe_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I]),
     "tkmc_fe_count": (_I, [_P, _I64, _I64, _I64, _I, _P, _I, _P, _P, _SZ, _P, _P]),
     "tkmc_fe_emit": (_I, [_P, _I64, _I64, _I64, _I, _I64, _P, _P, _I, _P, _P, _SZ,
-                          _P, _P, _P, _P, _P, _P]),
+                          _P, _P, _P, _P, _I64, _P, _I64, _P]),
+    "tkmc_fe_check": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P]),
     "tkmc_fe_classify": (_I, [_P, _I64, _I64, _I64, _P, _I, _P, _SZ, _P]),
     "tkmc_fe_scan": (_I, [_I64, _I64, _I64, _I, _I, _P, _P, _SZ, _P]),
     "tkmc_fe_read_counts": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P, _P]),

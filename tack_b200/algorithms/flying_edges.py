@@ -262,8 +262,15 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
             _lib.check(lib.tkmc_fe_emit(
                 b.scalar.data_ptr(), g.nx, g.ny, g.nz, 0, 0, _geom6(g), _f32_array(grp),
                 len(grp), b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(),
-                ws.numel(), ida, ida, _i64_array(tri_base), points_t.data_ptr(),
-                conn_t.data_ptr(), stream), "tkmc_fe_emit")
+                ws.numel(), ida, ida, _i64_array(tri_base), points_t.data_ptr(), total_points,
+                conn_t.data_ptr(), total_tris, stream), "tkmc_fe_emit")
+    # Surface any error the kernels recorded (bounded waits, capacity).
+    for b in bl:
+        g = b.grid
+        for gi, grp in enumerate(groups):
+            _, ws = b.counts[gi]
+            _lib.check(lib.tkmc_fe_check(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(), ws.numel(),
+                                         stream), "tkmc_fe_check")
 
     points_field = Field(f32, (total_points * 3,), CUDABuffer(points_t))
     conn_field = Field(i32, (total_tris * 3,), CUDABuffer(conn_t))

@@ -104,7 +104,6 @@ __constant__ uint64_t c_case_tris[256] = {TKMC_CASE_LIST(TKMC_PACK_CASE)};
 #undef TKMC_PACK_CASE
 
 constexpr int kThreads = 256;
-constexpr int kRowsPerTile = 256;  // K2 tile: one row per thread in the scan
 constexpr int kScanItems = 16;     // generic scan: items per thread
 constexpr int kScanTile = kThreads * kScanItems;
 
@@ -179,14 +178,18 @@ __device__ __forceinline__ uint32_t spread8(uint32_t x) {
 //
 // Tile t publishes flags[t] = 1 with its aggregate, then flags[t] = 2 with
 // its inclusive prefix.  Called by all 32 lanes of one warp; every lane
-// returns the exclusive prefix.  A wait longer than wait_ns (measured with
-// %globaltimer) gives up, records TKMC_ERR_DEVICE_TIMEOUT in *err and
-// publishes anyway so later tiles do not wait on this one.
+// returns the exclusive prefix.  Each round inspects the 128 nearest
+// unresolved predecessors (4 per lane): it sums aggregates back to the
+// nearest inclusive prefix, or over all 128 and continues further back.  A
+// wait longer than wait_ns (measured with %globaltimer) gives up, records
+// TKMC_ERR_DEVICE_TIMEOUT in *err and publishes anyway so later tiles do
+// not wait on this one.
 template <int K>
 __device__ void lookback(uint32_t* flags, long long* agg, long long* incl,
                          int64_t tile, const long long (&aggregate)[K],
                          long long (&prefix)[K], int64_t wait_ns,
                          bool skip_publish, long long* err) {
+  constexpr int kPer = 4;  // predecessors per lane and round
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int k = 0; k < K; ++k) prefix[k] = 0;
@@ -200,12 +203,26 @@ __device__ void lookback(uint32_t* flags, long long* agg, long long* incl,
     int64_t pred = tile - 1;
     uint64_t t0 = 0;
     while (true) {
-      const int64_t idx = pred - lane;
-      const uint32_t f = idx >= 0 ? ld_acquire_u32(flags + idx) : 2u;
-      const uint32_t m2 = __ballot_sync(0xffffffffu, f == 2u);
-      const uint32_t m0 = __ballot_sync(0xffffffffu, f == 0u);
-      const uint32_t need = m2 ? (((m2 & (0u - m2)) << 1) - 1u) : 0xffffffffu;
-      if (m0 & need) {
+      // Position p = kPer*lane + i is predecessor pred - p (p = 0 nearest).
+      uint32_t f[kPer];
+      int first2 = kPer, any0_before = 0;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int64_t idx = pred - (kPer * lane + i);
+        f[i] = idx >= 0 ? ld_acquire_u32(flags + idx) : 2u;
+      }
+#pragma unroll
+      for (int i = kPer - 1; i >= 0; --i)
+        if (f[i] == 2u) first2 = i;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i)
+        if (f[i] == 0u && i < first2) any0_before = 1;
+      const uint32_t m2 = __ballot_sync(0xffffffffu, first2 < kPer);
+      const int L2 = m2 ? __ffs(m2) - 1 : 32;  // lane holding the nearest inclusive
+      // Not ready if a flag-0 predecessor is nearer than the nearest inclusive.
+      const bool blocking = (lane < L2 && any0_before) ||
+                            (lane == L2 && any0_before);
+      if (__any_sync(0xffffffffu, blocking)) {
         uint64_t now = 0;
         if (lane == 0) now = global_ns();
         now = __shfl_sync(0xffffffffu, now, 0);
@@ -217,18 +234,24 @@ __device__ void lookback(uint32_t* flags, long long* agg, long long* incl,
         __nanosleep(64);
         continue;
       }
-      const int first2 = m2 ? __ffs(m2) - 1 : 32;
-      const bool take = ((need >> lane) & 1u) && idx >= 0;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         long long v = 0;
-        if (take) v = (lane == first2) ? __ldcg(incl + idx * K + k) : __ldcg(agg + idx * K + k);
+#pragma unroll
+        for (int i = 0; i < kPer; ++i) {
+          const int64_t idx = pred - (kPer * lane + i);
+          if (idx < 0) continue;
+          if (lane < L2 || (lane == L2 && i < first2))
+            v += __ldcg(agg + idx * K + k);
+          else if (lane == L2 && i == first2)
+            v += __ldcg(incl + idx * K + k);
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         prefix[k] += v;
       }
       if (m2) break;
-      pred -= 32;
+      pred -= 32 * kPer;
     }
   }
   if (lane == 0 && !skip_publish) {
@@ -339,17 +362,23 @@ struct FeDims {
   int64_t R;            // node rows = M * N
   int64_t n_own_rows;   // rows this slab owns (R, or R - M with a ghost plane)
   int64_t nx, ny;       // cells per row, cell rows per plane (mask index)
-  int64_t ntiles;       // K2 tiles
+  int64_t ntiles;       // K2b scan tiles
+  int64_t ctiles;       // K2a count tiles
   int W;                // 32-bit words per row
   int S, logS;          // lanes per row (power of two <= 32)
+  int TR;               // K2 tile height in rows
+  int logP;             // K2 threads per row = 1 << logP (TR << logP == block size)
+  int S3, logS3;        // K3 lanes per row (<= 8: several rows per warp)
 };
 
 // Per-isovalue workspace views.
 struct FeIsoWs {
   uint32_t* bits;       // flat node bitmask
+  int* cnt;             // [R][4] row counts X, Y, Z, T
+  long long* tot;       // [4] this slab's own totals (contiguous across isovalues)
   long long* rowoff;    // [R][4] exclusive offsets X, Y, Z, T (section-relative)
   uint32_t* work;       // active own rows
-  uint32_t* flags;      // [ntiles]
+  uint32_t* flags;      // [ntiles] (scan tiles of kScanRows rows)
   long long* agg;       // [ntiles][4]
   long long* incl;      // [ntiles][4]
   long long* info;      // [16]: 0-3 own totals, 4-7 all-row totals, 8 active rows,
@@ -370,8 +399,8 @@ struct Quad {
 // Lanes sl of one S-lane row segment hold words w = w0 + sl.  Fills the next
 // word of each row from the neighbouring lane, or loads it at the segment end.
 __device__ __forceinline__ void load_quad(Quad& q, const uint32_t* __restrict__ bits,
-                                          const FeDims& d, int64_t rowbit, int w, int sl,
-                                          bool valid, bool hasY, bool hasZ) {
+                                          const FeDims& d, int S, int64_t rowbit, int w,
+                                          int sl, bool valid, bool hasY, bool hasZ) {
   const int64_t L = d.L;
   const int64_t plane = d.L * d.M;
   const bool hasC = hasY && hasZ;
@@ -379,11 +408,11 @@ __device__ __forceinline__ void load_quad(Quad& q, const uint32_t* __restrict__ 
   q.b = hasY ? row_word(bits, rowbit + L, w, L) : 0u;
   q.c = hasZ ? row_word(bits, rowbit + plane, w, L) : 0u;
   q.d = hasC ? row_word(bits, rowbit + plane + L, w, L) : 0u;
-  q.an = __shfl_down_sync(0xffffffffu, q.a, 1, d.S);
-  q.bn = __shfl_down_sync(0xffffffffu, q.b, 1, d.S);
-  q.cn = __shfl_down_sync(0xffffffffu, q.c, 1, d.S);
-  q.dn = __shfl_down_sync(0xffffffffu, q.d, 1, d.S);
-  if (sl == d.S - 1) {
+  q.an = __shfl_down_sync(0xffffffffu, q.a, 1, S);
+  q.bn = __shfl_down_sync(0xffffffffu, q.b, 1, S);
+  q.cn = __shfl_down_sync(0xffffffffu, q.c, 1, S);
+  q.dn = __shfl_down_sync(0xffffffffu, q.d, 1, S);
+  if (sl == S - 1) {
     const bool more = (w + 1) < d.W;
     q.an = (valid && more) ? row_word(bits, rowbit, w + 1, L) : 0u;
     q.bn = (hasY && more) ? row_word(bits, rowbit + L, w + 1, L) : 0u;
@@ -411,154 +440,355 @@ __device__ __forceinline__ uint32_t active_cells(const Quad& q, uint32_t xcell_m
 // ------------------------------------------------------------------------
 // K2: per-row counts + single-pass scan + worklist
 // ------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads)
-k_fe_count_scan(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t wait_ns,
-                int64_t skip_tile) {
-  __shared__ int s_cnt[4][kRowsPerTile];
+//
+// A tile is TR consecutive node rows (linear order r = k*M + j).  Its bit
+// rows [R0, R0+TR] and their next-plane neighbours [R0+M, R0+M+TR] are
+// staged in shared memory with coalesced loads (each is one contiguous run
+// of the flat bitmask), so the counting touches no global memory.  Rows are
+// handled by S-lane segments (S words per pass); per-row totals are reduced
+// in the segment, scanned across the tile, and chained across tiles by the
+// decoupled look-back.
+
+// Word w of the row whose first node sits at bit rb of the staged run s.
+__device__ __forceinline__ uint32_t sm_row_word(const uint32_t* s, int64_t rb, int w,
+                                                int64_t L) {
+  const int64_t rem = L - 32 * (int64_t)w;
+  if (rem <= 0) return 0u;
+  const int64_t pos = rb + 32 * (int64_t)w;
+  const int64_t q = pos >> 5;
+  const int sh = (int)(pos & 31);
+  uint32_t x = s[q];
+  if (sh) x = __funnelshift_r(x, s[q + 1], sh);
+  if (rem < 32) x &= (1u << rem) - 1u;
+  return x;
+}
+
+// Words reserved per staged run: the run itself, the 16-byte alignment
+// shift in front of it and the rounding of the last 16-byte copy.
+__device__ __forceinline__ int64_t k2_stage_words(const FeDims& d) {
+  return (((int64_t)(d.TR + 1) * d.W + 3 + 8) + 3) & ~(int64_t)3;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// Copy bitmask words [first, first + words) into s with 16-byte cp.async
+// copies from the 16-byte boundary at or below `first`; returns the index in
+// s of word `first`.  The bitmask has >= 8 zero padding words, so the
+// rounded-up tail stays inside the allocation.
+__device__ __forceinline__ int stage_run(uint32_t* s, const uint32_t* bits, int64_t first,
+                                         int64_t words) {
+  const int64_t g0 = first & ~(int64_t)3;
+  const int shift = (int)(first - g0);
+  const int64_t nvec = (shift + words + 3) >> 2;
+  for (int64_t i = threadIdx.x; i < nvec; i += kThreads) cp_async16(s + 4 * i, bits + g0 + 4 * i);
+  return shift;
+}
+
+// Word w of the row whose first node is bit b of the staged run s (zero
+// beyond the row's length L), and bit 0 of word w + 1 in *next0.
+__device__ __forceinline__ uint32_t staged_word(const uint32_t* s, int b, int w, int L,
+                                                uint32_t* next0) {
+  const int rem = L - 32 * w;
+  if (rem <= 0) {
+    *next0 = 0u;
+    return 0u;
+  }
+  const int pos = b + 32 * w;
+  const int q = pos >> 5, sh = pos & 31;
+  const uint32_t lo = s[q], hi = s[q + 1];
+  uint32_t x = sh ? __funnelshift_r(lo, hi, sh) : lo;
+  *next0 = rem > 32 ? (hi >> sh) & 1u : 0u;
+  if (rem < 32) x &= (1u << rem) - 1u;
+  return x;
+}
+
+// Triangles of the (up to 32) cells of one word, bit-parallel.  For every
+// case of the marching-cubes table, triangles = V - 2F - 4*belt + 4*full,
+// where V counts corners above the isovalue, F the faces with all four
+// corners above, belt is 1 when exactly two antipodal corners are below, and
+// full is 1 when all eight are above.  (It is #cut edges - 2 * #components
+// of the above corners, with the cube graph's two kinds of non-face cycles
+// corrected; checked against all 256 table entries.)  Corner words:
+// 0 a, 1 a1, 2 b1, 3 b, 4 c, 5 c1, 6 d1, 7 d; xm selects the valid cells.
+__device__ __forceinline__ unsigned tri_count_word(uint32_t a, uint32_t a1, uint32_t b,
+                                                   uint32_t b1, uint32_t c, uint32_t c1,
+                                                   uint32_t d, uint32_t d1, uint32_t xm) {
+  const unsigned V = __popc(a & xm) + __popc(a1 & xm) + __popc(b & xm) + __popc(b1 & xm) +
+                     __popc(c & xm) + __popc(c1 & xm) + __popc(d & xm) + __popc(d1 & xm);
+  const uint32_t ab = a & b, a1b1 = a1 & b1, cd = c & d, c1d1 = c1 & d1;
+  const uint32_t f0 = ab & a1b1;        // corners 0 1 2 3
+  const uint32_t f1 = cd & c1d1;        // 4 5 6 7
+  const uint32_t f2 = a & a1 & c & c1;  // 0 1 5 4
+  const uint32_t f3 = b & b1 & d & d1;  // 3 2 6 7
+  const uint32_t f4 = ab & cd;          // 0 3 7 4
+  const uint32_t f5 = a1b1 & c1d1;      // 1 2 6 5
+  const unsigned F = __popc(f0 & xm) + __popc(f1 & xm) + __popc(f2 & xm) + __popc(f3 & xm) +
+                     __popc(f4 & xm) + __popc(f5 & xm);
+  const uint32_t full = f0 & f1 & xm;
+  const uint32_t belt = (~a & ~d1 & a1 & b1 & b & c & c1 & d) |   // 0 and 6 below
+                        (~a1 & ~d & a & b1 & b & c & c1 & d1) |   // 1 and 7
+                        (~b1 & ~c & a & a1 & b & c1 & d1 & d) |   // 2 and 4
+                        (~b & ~c1 & a & a1 & b1 & c & d1 & d);    // 3 and 5
+  return V - 2 * F - 4 * __popc(belt & xm) + 4 * __popc(full);
+}
+
+// Counts of one row over words [wbeg, wbeg + WP) visited from word wbeg + rot
+// (rotation keeps the threads of a warp on different banks).  ALIGNED: the
+// row length is a multiple of 32 nodes, so every row starts on a word.
+template <bool ALIGNED>
+__device__ __forceinline__ void count_row_words(
+    const uint32_t* sAr, const uint32_t* sCr, int ba, int bb, int bc, int bd, int Li, int W,
+    int wbeg, int WP, int rot, bool hasY, bool hasZ, const int* s_ntri,
+    const int32_t* __restrict__ mask, int64_t cell_row0, unsigned& cX, unsigned& cY,
+    unsigned& cZ, unsigned& cT) {
+  const bool hasC = hasY && hasZ;
+  int wl = rot;
+#pragma unroll 4
+  for (int i = 0; i < WP; ++i) {
+    const int w = wbeg + wl;
+    wl = (wl + 1 == WP) ? 0 : wl + 1;
+    if (w >= W) continue;
+    uint32_t a, an, b = 0, bn = 0, c = 0, cn = 0, dd = 0, dn = 0;
+    if (ALIGNED) {
+      const bool more = w + 1 < W;
+      const int qa = (ba >> 5) + w;
+      a = sAr[qa];
+      an = more ? (sAr[qa + 1] & 1u) : 0u;
+      if (hasY) { const int q = (bb >> 5) + w; b = sAr[q]; bn = more ? (sAr[q + 1] & 1u) : 0u; }
+      if (hasZ) { const int q = (bc >> 5) + w; c = sCr[q]; cn = more ? (sCr[q + 1] & 1u) : 0u; }
+      if (hasC) { const int q = (bd >> 5) + w; dd = sCr[q]; dn = more ? (sCr[q + 1] & 1u) : 0u; }
+    } else {
+      a = staged_word(sAr, ba, w, Li, &an);
+      if (hasY) b = staged_word(sAr, bb, w, Li, &bn);
+      if (hasZ) c = staged_word(sCr, bc, w, Li, &cn);
+      if (hasC) dd = staged_word(sCr, bd, w, Li, &dn);
+    }
+    const uint32_t xm = low_mask(Li - 1 - 32 * w);
+    const uint32_t a1 = (a >> 1) | (an << 31);
+    cX += __popc((a ^ a1) & xm);
+    if (hasY) cY += __popc(a ^ b);
+    if (hasZ) cZ += __popc(a ^ c);
+    if (hasC) {
+      const uint32_t b1 = (b >> 1) | (bn << 31), c1 = (c >> 1) | (cn << 31);
+      const uint32_t d1 = (dd >> 1) | (dn << 31);
+      cT += tri_count_word(a, a1, b, b1, c, c1, dd, d1, xm);
+      if (mask) {  // masked cells emit nothing: take their triangles back out
+        const uint32_t u = (a ^ b) | (a ^ c) | (a ^ dd);
+        const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
+        uint32_t act = (u | (u >> 1) | (un << 31) | (a ^ a1)) & xm;
+        while (act) {
+          const int bit = __ffs(act) - 1;
+          act &= act - 1;
+          if (__ldg(mask + cell_row0 + 32 * w + bit) != 0)
+            cT -= s_ntri[cell_case(bit, a, a1, b, b1, c, c1, dd, d1)];
+        }
+      }
+    }
+  }
+}
+
+// K2a: per-row counts {X, Y, Z, T} of one tile of TR rows -> cnt[R][4].
+// Tiles are independent (no inter-tile waits).
+__global__ void __launch_bounds__(kThreads, 3)
+k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nwords) {
+  extern __shared__ uint32_t k2_smem[];
   __shared__ int s_ntri[256];
+  const FeIsoWs& W = ws.iso[blockIdx.y];
+  const int tid = threadIdx.x;
+  const int64_t stage = k2_stage_words(d);
+  uint32_t* sA = k2_smem;
+  uint32_t* sC = k2_smem + stage;
+  s_ntri[tid] = (int)(c_case_tris[tid] >> 60);
+  const int TR = d.TR;
+  const int64_t R0 = (int64_t)blockIdx.x * TR;
+  const int64_t L = d.L;
+
+  // Stage the two runs of bit rows (all copies in flight at once).
+  const int64_t a_first = (R0 * L) >> 5;
+  const int64_t a_last_row = min(R0 + TR + 1, d.R);
+  const int64_t a_words = min(((a_last_row * L + 31) >> 5) + 1, nwords + 1) - a_first;
+  const uint32_t* sAr = sA + stage_run(sA, W.bits, a_first, a_words);
+  const int64_t c_row0 = R0 + d.M;
+  int64_t c_first = 0;
+  const uint32_t* sCr = sC;
+  if (c_row0 < d.R) {
+    c_first = (c_row0 * L) >> 5;
+    const int64_t c_last_row = min(c_row0 + TR + 1, d.R);
+    const int64_t c_words = min(((c_last_row * L + 31) >> 5) + 1, nwords + 1) - c_first;
+    sCr = sC + stage_run(sC, W.bits, c_first, c_words);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // Thread (row, part): P threads per row, each over a contiguous share of
+  // the row's words.
+  const int P = 1 << d.logP;
+  const int row_local = tid >> d.logP, part = tid & (P - 1);
+  const int64_t r = R0 + row_local;
+  const bool valid = r < d.R;
+  const uint32_t r32 = (uint32_t)r, M32 = (uint32_t)d.M;
+  const uint32_t j = valid ? r32 % M32 : 0u, k = valid ? r32 / M32 : 0u;
+  const bool hasY = valid && (j + 1 < M32);
+  const bool hasZ = valid && ((int64_t)k + 1 < d.N);
+  const int Li = (int)L;
+  const int ba = (int)(r * L - a_first * 32), bb = ba + Li;
+  const int bc = (int)((r + d.M) * L - c_first * 32), bd = bc + Li;
+  unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
+  if (valid) {
+    const int WP = (d.W + P - 1) >> d.logP;
+    const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
+    if ((L & 31) == 0)
+      count_row_words<true>(sAr, sCr, ba, bb, bc, bd, Li, d.W, part * WP, WP, row_local % WP,
+                            hasY, hasZ, s_ntri, mask, cell_row0, cX, cY, cZ, cT);
+    else
+      count_row_words<false>(sAr, sCr, ba, bb, bc, bd, Li, d.W, part * WP, WP, row_local % WP,
+                             hasY, hasZ, s_ntri, mask, cell_row0, cX, cY, cZ, cT);
+  }
+  for (int o = P >> 1; o > 0; o >>= 1) {
+    cX += __shfl_xor_sync(0xffffffffu, cX, o);
+    cY += __shfl_xor_sync(0xffffffffu, cY, o);
+    cZ += __shfl_xor_sync(0xffffffffu, cZ, o);
+    cT += __shfl_xor_sync(0xffffffffu, cT, o);
+  }
+  if (part == 0 && valid)
+    reinterpret_cast<int4*>(W.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
+}
+
+// K2b: single-pass (decoupled look-back) exclusive scan of the row counts
+// into row offsets, totals and the worklist of active own rows.  A tile is
+// kScanRows rows, 4 consecutive rows per thread.
+constexpr int kScanRowsPerThread = 4;
+constexpr int kScanRows = kThreads * kScanRowsPerThread;
+
+__global__ void __launch_bounds__(kThreads)
+k_fe_scan_rows(FeDims d, FeWsAll ws, int64_t wait_ns, int64_t skip_tile) {
   __shared__ long long s_wtot[4][kThreads / 32];
   __shared__ long long s_prefix[4];
   __shared__ int64_t s_tile;
   __shared__ unsigned s_wbase[kThreads / 32];
-
   const FeIsoWs& W = ws.iso[blockIdx.y];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  s_ntri[tid] = (int)(c_case_tris[tid] >> 60);
   if (tid == 0) s_tile = (int64_t)atomicAdd((unsigned long long*)(W.info + 9), 1ull);
   __syncthreads();
   const int64_t tile = s_tile;
-  const int64_t row0 = tile * kRowsPerTile;
-  const int S = d.S, G = 32 >> d.logS;
-  const int seg = lane >> d.logS, sl = lane & (S - 1);
+  const int64_t r0 = tile * kScanRows + (int64_t)tid * kScanRowsPerThread;
 
-  for (int p = 0; p < S; ++p) {
-    const int local = ((p << 3) + warp) * G + seg;
-    const int64_t r = row0 + local;
-    const bool valid = r < d.R;
-    const int64_t j = valid ? r % d.M : 0, k = valid ? r / d.M : 0;
-    const bool hasY = valid && (j + 1 < d.M);
-    const bool hasZ = valid && (k + 1 < d.N);
-    const bool hasC = hasY && hasZ;
-    const int64_t rowbit = r * d.L;
-    unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
-    for (int w0 = 0; w0 < d.W; w0 += S) {
-      const int w = w0 + sl;
-      Quad q;
-      load_quad(q, W.bits, d, rowbit, w, sl, valid, hasY, hasZ);
-      const uint32_t xm = low_mask((int)(d.L - 1 - 32 * (int64_t)w));
-      cX += __popc((q.a ^ shr1(q.a, q.an)) & xm);
-      if (hasY) cY += __popc(q.a ^ q.b);
-      if (hasZ) cZ += __popc(q.a ^ q.c);
-      if (hasC) {
-        uint32_t act = active_cells(q, xm);
-        if (act) {
-          const uint32_t a1 = shr1(q.a, q.an), b1 = shr1(q.b, q.bn);
-          const uint32_t c1 = shr1(q.c, q.cn), d1 = shr1(q.d, q.dn);
-          while (act) {
-            const int b = __ffs(act) - 1;
-            act &= act - 1;
-            int nt = s_ntri[cell_case(b, q.a, a1, q.b, b1, q.c, c1, q.d, d1)];
-            if (nt && mask) {
-              const int64_t cell = (k * d.ny + j) * d.nx + 32 * (int64_t)w + b;
-              if (__ldg(mask + cell) != 0) nt = 0;
-            }
-            cT += nt;
-          }
-        }
-      }
-    }
-    for (int o = S >> 1; o > 0; o >>= 1) {
-      cX += __shfl_xor_sync(0xffffffffu, cX, o);
-      cY += __shfl_xor_sync(0xffffffffu, cY, o);
-      cZ += __shfl_xor_sync(0xffffffffu, cZ, o);
-      cT += __shfl_xor_sync(0xffffffffu, cT, o);
-    }
-    if (sl == 0) {
-      s_cnt[0][local] = (int)cX;
-      s_cnt[1][local] = (int)cY;
-      s_cnt[2][local] = (int)cZ;
-      s_cnt[3][local] = (int)cT;
-    }
-  }
-  __syncthreads();
-
-  // Block-wide exclusive scan of the tile's 256 rows (thread tid <-> row tid).
-  long long own[4], inc[4];
+  int4 c[kScanRowsPerThread];
+  long long own[4] = {0, 0, 0, 0};
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    own[c] = s_cnt[c][tid];
-    long long x = own[c];
+  for (int i = 0; i < kScanRowsPerThread; ++i) {
+    c[i] = (r0 + i < d.R) ? __ldcg(reinterpret_cast<const int4*>(W.cnt) + r0 + i)
+                          : make_int4(0, 0, 0, 0);
+    own[0] += c[i].x; own[1] += c[i].y; own[2] += c[i].z; own[3] += c[i].w;
+  }
+  long long inc[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    long long x = own[q];
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const long long y = __shfl_up_sync(0xffffffffu, x, o);
       if (lane >= o) x += y;
     }
-    inc[c] = x;
-    if (lane == 31) s_wtot[c][warp] = x;
+    inc[q] = x;
+    if (lane == 31) s_wtot[q][warp] = x;
   }
   __syncthreads();
   long long tile_total[4];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int q = 0; q < 4; ++q) {
     long long before = 0, all = 0;
 #pragma unroll
     for (int w2 = 0; w2 < kThreads / 32; ++w2) {
-      const long long t = s_wtot[c][w2];
+      const long long t = s_wtot[q][w2];
       if (w2 < warp) before += t;
       all += t;
     }
-    inc[c] += before;
-    tile_total[c] = all;
+    inc[q] += before;
+    tile_total[q] = all;
   }
   if (warp == 0) {
     long long pre[4];
-    lookback<4>(W.flags, W.agg, W.incl, tile, tile_total, pre, wait_ns,
-                tile == skip_tile, W.info + 10);
+    lookback<4>(W.flags, W.agg, W.incl, tile, tile_total, pre, wait_ns, tile == skip_tile,
+                W.info + 10);
     if (lane == 0)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) s_prefix[c] = pre[c];
+      for (int q = 0; q < 4; ++q) s_prefix[q] = pre[q];
   }
   __syncthreads();
 
-  const int64_t r = row0 + tid;
   long long ex[4];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) ex[c] = s_prefix[c] + inc[c] - own[c];
-  if (r < d.R) {
-    longlong2* dst = reinterpret_cast<longlong2*>(W.rowoff + r * 4);
-    dst[0] = make_longlong2(ex[0], ex[1]);
-    dst[1] = make_longlong2(ex[2], ex[3]);
-    if (r == d.n_own_rows)
+  for (int q = 0; q < 4; ++q) ex[q] = s_prefix[q] + inc[q] - own[q];
+  unsigned act_bits = 0;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) W.info[c] = ex[c];
-    if (r == d.R - 1) {
+  for (int i = 0; i < kScanRowsPerThread; ++i) {
+    const int64_t rr = r0 + i;
+    if (rr < d.R) {
+      longlong2* dst = reinterpret_cast<longlong2*>(W.rowoff + rr * 4);
+      dst[0] = make_longlong2(ex[0], ex[1]);
+      dst[1] = make_longlong2(ex[2], ex[3]);
+      // Own totals: the offset of the first ghost row, or the grand total.
+      if (rr == d.n_own_rows)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        W.info[4 + c] = ex[c] + own[c];
-        if (d.n_own_rows == d.R) W.info[c] = ex[c] + own[c];
+        for (int q = 0; q < 4; ++q) W.info[q] = W.tot[q] = ex[q];
+      if (rr < d.n_own_rows && (c[i].x | c[i].y | c[i].z | c[i].w) != 0) act_bits |= 1u << i;
+    }
+    ex[0] += c[i].x; ex[1] += c[i].y; ex[2] += c[i].z; ex[3] += c[i].w;
+    if (rr == d.R - 1) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        W.info[4 + q] = ex[q];
+        if (d.n_own_rows == d.R) W.info[q] = W.tot[q] = ex[q];
       }
     }
   }
   // Worklist of own rows with any output (order is irrelevant: every row
   // writes at its own offsets).
-  const bool active = r < d.n_own_rows && (own[0] | own[1] | own[2] | own[3]) != 0;
-  const uint32_t bal = __ballot_sync(0xffffffffu, active);
-  if (lane == 0 && bal)
+  const unsigned nact = __popc(act_bits);
+  unsigned incl_n = nact;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, incl_n, o);
+    if (lane >= o) incl_n += y;
+  }
+  const unsigned wtotal = __shfl_sync(0xffffffffu, incl_n, 31);
+  if (lane == 31 && wtotal)
     s_wbase[warp] = (unsigned)atomicAdd((unsigned long long*)(W.info + 8),
-                                        (unsigned long long)__popc(bal));
+                                        (unsigned long long)wtotal);
   __syncwarp();
-  if (active) W.work[s_wbase[warp] + __popc(bal & ((1u << lane) - 1u))] = (uint32_t)r;
+  if (nact) {
+    unsigned pos = s_wbase[warp] + incl_n - nact;
+    for (int i = 0; i < kScanRowsPerThread; ++i)
+      if (act_bits & (1u << i)) W.work[pos++] = (uint32_t)(r0 + i);
+  }
 }
 
 // ------------------------------------------------------------------------
 // K3: emit points and triangles of the active rows
 // ------------------------------------------------------------------------
+//
+// Phase 1 (lane = one 32-node word of a row, S lanes per row): load the four
+// bit rows around the word, form the crossing masks and the active-cell mask,
+// and scan the per-word crossing counts across the row.  Each word's masks,
+// bits and absolute offsets go to a shared-memory record.
+// Phase 2 (lane = one node/cell of a word): loop over the words with output;
+// all 32 lanes emit that word together -- one coalesced 128-byte read of the
+// row's values, contiguous point stores, and one triangle scan per word.
 
 struct FeEmitArgs {
   const float* v;
   const int32_t* mask;
   float* points;
   int32_t* conn;
+  long long points_cap, conn_cap;  // rows of 3
   float geom[6];
   int64_t k_offset;
   IsoParams iso;
@@ -566,6 +796,12 @@ struct FeEmitArgs {
   long long pt_out_base[TKMC_MAX_ISO][3];
   long long tri_out_base[TKMC_MAX_ISO];
 };
+
+// An emit write that would land outside the caller's buffers is skipped and
+// recorded in the workspace error word (read by tkmc_fe_check).
+__device__ __forceinline__ void record_overflow(long long* info) {
+  atomicExch((unsigned long long*)(info + 10), (unsigned long long)TKMC_ERR_CAPACITY);
+}
 
 // Segmented (width S) inclusive scan.
 __device__ __forceinline__ unsigned seg_scan(unsigned x, int sl, int S) {
@@ -576,198 +812,288 @@ __device__ __forceinline__ unsigned seg_scan(unsigned x, int sl, int S) {
   return x;
 }
 
-__global__ void __launch_bounds__(kThreads)
+// Word record layout in shared memory (32-bit words; odd stride).
+//   0-7   crossing masks of the 8 edge groups: x(a) y(a) z(a) x(b) x(c) x(d) y(c) z(b)
+//   8     cells with triangles (before the mask)
+//   9-16  bit words a a1 b b1 c c1 d d1 (x1 = next node)
+//   17-32 int64 id offset of each group's first crossing in this word (lo, hi)
+//   33-34 int64 triangle offset of the row
+//   35-36 j, k of the row
+//   37-38 exclusive prefix over the warp's words of points / active cells
+constexpr int kRec = 39;
+constexpr int kRecMasks = 0, kRecAct = 8, kRecBits = 9, kRecOff = 17, kRecTri = 33, kRecJ = 35,
+              kRecK = 36, kRecPB = 37, kRecCB = 38;
+
+// Edge e -> (group, +1 node) as nibble g | plus << 3 (edges 0..11).
+constexpr uint64_t kEdgeGroup = 0x0ull | (0x9ull << 4) | (0x3ull << 8) | (0x1ull << 12) |
+                                (0x4ull << 16) | (0xEull << 20) | (0x5ull << 24) |
+                                (0x6ull << 28) | (0x2ull << 32) | (0xAull << 36) |
+                                (0x7ull << 40) | (0xFull << 44);
+
+__device__ __forceinline__ long long rec_i64(const uint32_t* rec, int at) {
+  return (long long)(((unsigned long long)rec[at + 1] << 32) | rec[at]);
+}
+__device__ __forceinline__ void rec_put_i64(uint32_t* rec, int at, long long v) {
+  rec[at] = (uint32_t)(unsigned long long)v;
+  rec[at + 1] = (uint32_t)((unsigned long long)v >> 32);
+}
+
+// Position of the k-th (0-based) set bit of m; k < popc(m).
+__device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
+  int pos = 0;
+#pragma unroll
+  for (int sft = 16; sft >= 1; sft >>= 1) {
+    const int low = __popc(m & ((1u << sft) - 1u));
+    if (k >= low) {
+      k -= low;
+      m >>= sft;
+      pos += sft;
+    }
+  }
+  return pos;
+}
+
+// Largest word u of the warp whose record field `field` (non-decreasing in u)
+// is <= e.
+__device__ __forceinline__ int find_word(const uint32_t* recs, int field, unsigned e) {
+  int lo = 0;
+#pragma unroll
+  for (int step = 16; step >= 1; step >>= 1) {
+    const int m = lo + step;
+    if (m < 32 && recs[m * kRec + field] <= e) lo = m;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kThreads, 3)
 k_fe_emit(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
-  __shared__ int s_pid[12][kThreads];
+  __shared__ uint32_t s_rec[kThreads / 32][32 * kRec];
+  __shared__ long long s_tri[kThreads / 32][32];  // running triangle offset per row segment
   const int isoi = blockIdx.y;
   const FeIsoWs& W = ws.iso[isoi];
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_tris[tid];
   __syncthreads();
+  uint32_t* recs = s_rec[warp];
+  long long* tri_cur = s_tri[warp];
 
-  const int S = d.S, G = 32 >> d.logS;
-  const int seg = lane >> d.logS, sl = lane & (S - 1);
+  const int S = d.S3, logS = d.logS3, G = 32 >> logS;
+  const int seg = lane >> logS, sl = lane & (S - 1);
   const int64_t L = d.L, plane = d.L * d.M;
+  const uint32_t M32 = (uint32_t)d.M;
   const int64_t n_active = *((volatile long long*)(W.info + 8));
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const float iso = A.iso.v[isoi];
   const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
   const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idX = A.pt_id_base[isoi][0], idY = A.pt_id_base[isoi][1],
-                  idZ = A.pt_id_base[isoi][2];
-  const long long outX = A.pt_out_base[isoi][0], outY = A.pt_out_base[isoi][1],
-                  outZ = A.pt_out_base[isoi][2];
+  const long long idB[3] = {A.pt_id_base[isoi][0], A.pt_id_base[isoi][1],
+                            A.pt_id_base[isoi][2]};
+  const long long shiftX = A.pt_out_base[isoi][0] - idB[0];
+  const long long shiftY = A.pt_out_base[isoi][1] - idB[1];
+  const long long shiftZ = A.pt_out_base[isoi][2] - idB[2];
   const long long outT = A.tri_out_base[isoi];
 
   for (int64_t grp = gw; grp * G < n_active; grp += nw) {
+    // ---------------- phase 1: lane = (row segment, word) ----------------
     const int64_t item = grp * G + seg;
     const bool valid = item < n_active;
     const int64_t r = valid ? (int64_t)W.work[item] : 0;
-    const int64_t j = r % d.M, k = r / d.M;
-    const bool hasY = valid && (j + 1 < d.M);
-    const bool hasZ = valid && (k + 1 < d.N);
+    const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
+    const bool hasY = valid && (j + 1 < M32);
+    const bool hasZ = valid && ((int64_t)k + 1 < d.N);
     const bool hasC = hasY && hasZ;
     const int64_t rowbit = r * L;
-    // Row offsets (section-relative) of the four node rows and the cell row.
-    long long oxa = 0, oya = 0, oza = 0, ota = 0, oxb = 0, ozb = 0, oxc = 0, oyc = 0, oxd = 0;
+    long long off[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    long long ota = 0;
     if (valid) {
       const longlong2* ra = reinterpret_cast<const longlong2*>(W.rowoff + r * 4);
       const longlong2 p0 = ra[0], p1 = ra[1];
-      oxa = p0.x; oya = p0.y; oza = p1.x; ota = p1.y;
+      off[0] = p0.x + idB[0];
+      off[1] = p0.y + idB[1];
+      off[2] = p1.x + idB[2];
+      ota = p1.y;
     }
-    if (hasY) { oxb = W.rowoff[(r + 1) * 4 + 0]; ozb = W.rowoff[(r + 1) * 4 + 2]; }
-    if (hasZ) { oxc = W.rowoff[(r + d.M) * 4 + 0]; oyc = W.rowoff[(r + d.M) * 4 + 1]; }
-    if (hasC) oxd = W.rowoff[(r + d.M + 1) * 4 + 0];
-    const float py = coord(y0, j, hy);
-    const float pz = coord(z0, k + A.k_offset, hz);
-    const float py1 = coord(y0, j + 1, hy);
-    const float pz1 = coord(z0, k + 1 + A.k_offset, hz);
+    if (hasY) {
+      off[3] = W.rowoff[(r + 1) * 4 + 0] + idB[0];
+      off[7] = W.rowoff[(r + 1) * 4 + 2] + idB[2];
+    }
+    if (hasZ) {
+      off[4] = W.rowoff[(r + d.M) * 4 + 0] + idB[0];
+      off[6] = W.rowoff[(r + d.M) * 4 + 1] + idB[1];
+    }
+    if (hasC) off[5] = W.rowoff[(r + d.M + 1) * 4 + 0] + idB[0];
+    if (sl == 0) tri_cur[seg] = ota;
 
-    unsigned cxa = 0, cya = 0, cza = 0, cxb = 0, cxc = 0, cxd = 0, cyc = 0, czb = 0, ct = 0;
     for (int w0 = 0; w0 < d.W; w0 += S) {
       const int w = w0 + sl;
       Quad q;
-      load_quad(q, W.bits, d, rowbit, w, sl, valid, hasY, hasZ);
-      const uint32_t xm = low_mask((int)(L - 1 - 32 * (int64_t)w));
-      const uint32_t xa = (q.a ^ shr1(q.a, q.an)) & xm;
-      const uint32_t ya = hasY ? (q.a ^ q.b) : 0u;
-      const uint32_t za = hasZ ? (q.a ^ q.c) : 0u;
-      uint32_t xb = 0, xc = 0, xd = 0, yc = 0, zb = 0, act = 0;
-      uint32_t a1 = 0, b1 = 0, c1 = 0, d1 = 0;
-      unsigned nt_lane = 0;
-      if (hasC) {
-        a1 = shr1(q.a, q.an); b1 = shr1(q.b, q.bn);
-        c1 = shr1(q.c, q.cn); d1 = shr1(q.d, q.dn);
-        xb = (q.b ^ b1) & xm;
-        xc = (q.c ^ c1) & xm;
-        xd = (q.d ^ d1) & xm;
-        yc = q.c ^ q.d;
-        zb = q.b ^ q.d;
-        act = active_cells(q, xm);
-        uint32_t m = act;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          unsigned nt = (unsigned)(s_case[cell_case(b, q.a, a1, q.b, b1, q.c, c1, q.d, d1)] >> 60);
+      load_quad(q, W.bits, d, S, rowbit, w, sl, valid, hasY, hasZ);
+      const uint32_t xm = low_mask((int)min(L - 1 - 32 * (int64_t)w, (int64_t)32));
+      uint32_t m[8];
+      m[0] = (q.a ^ shr1(q.a, q.an)) & xm;
+      m[1] = hasY ? (q.a ^ q.b) : 0u;
+      m[2] = hasZ ? (q.a ^ q.c) : 0u;
+      m[3] = (q.b ^ shr1(q.b, q.bn)) & xm;
+      m[4] = (q.c ^ shr1(q.c, q.cn)) & xm;
+      m[5] = (q.d ^ shr1(q.d, q.dn)) & xm;
+      m[6] = hasC ? (q.c ^ q.d) : 0u;
+      m[7] = hasC ? (q.b ^ q.d) : 0u;
+      const uint32_t act = hasC ? active_cells(q, xm) : 0u;
+      // Per-row exclusive prefixes of the eight crossing counts, two per scan.
+      unsigned pk[4], ex[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        pk[t] = __popc(m[2 * t]) | (__popc(m[2 * t + 1]) << 16);
+        const unsigned inc = seg_scan(pk[t], sl, S);
+        ex[t] = inc - pk[t];
+        pk[t] = __shfl_sync(0xffffffffu, inc, S - 1, S);  // segment total
+      }
+      // Warp-wide prefixes of this row's points and active cells per word:
+      // the work lists of phase 2.
+      const unsigned np = __popc(m[0]) + __popc(m[1]) + __popc(m[2]);
+      const unsigned nc = __popc(act);
+      unsigned wl = np | (nc << 16);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, wl, o);
+        if (lane >= o) wl += y;
+      }
+      const unsigned wtot = __shfl_sync(0xffffffffu, wl, 31);
+      const unsigned NP = wtot & 0xffffu, NC = wtot >> 16;
+      wl -= np | (nc << 16);
+      uint32_t* rec = recs + lane * kRec;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        rec[kRecMasks + g] = m[g];
+        const unsigned e = (g & 1) ? (ex[g >> 1] >> 16) : (ex[g >> 1] & 0xffffu);
+        rec_put_i64(rec, kRecOff + 2 * g, off[g] + e);
+      }
+      rec[kRecAct] = act;
+      rec[kRecBits + 0] = q.a; rec[kRecBits + 1] = shr1(q.a, q.an);
+      rec[kRecBits + 2] = q.b; rec[kRecBits + 3] = shr1(q.b, q.bn);
+      rec[kRecBits + 4] = q.c; rec[kRecBits + 5] = shr1(q.c, q.cn);
+      rec[kRecBits + 6] = q.d; rec[kRecBits + 7] = shr1(q.d, q.dn);
+      rec[kRecJ] = j;
+      rec[kRecK] = k;
+      rec[kRecPB] = wl & 0xffffu;
+      rec[kRecCB] = wl >> 16;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {  // carry the row totals into the next chunk
+        const unsigned t = (g & 1) ? (pk[g >> 1] >> 16) : (pk[g >> 1] & 0xffffu);
+        off[g] += t;
+      }
+      __syncwarp();
+
+      // ---------------- phase 2a: points, lane = one crossing ----------------
+      for (unsigned e0 = 0; e0 < NP; e0 += 32) {
+        const unsigned e = e0 + lane;
+        if (e < NP) {
+          const int u = find_word(recs, kRecPB, e);
+          const uint32_t* R = recs + u * kRec;
+          int kk = (int)(e - R[kRecPB]);
+          const uint32_t m0 = R[0], m1 = R[1], m2 = R[2];
+          const int c0 = __popc(m0), c1 = __popc(m1);
+          int type;
+          uint32_t mm;
+          if (kk < c0) {
+            type = 0; mm = m0;
+          } else if (kk < c0 + c1) {
+            type = 1; mm = m1; kk -= c0;
+          } else {
+            type = 2; mm = m2; kk -= c0 + c1;
+          }
+          const int bit = nth_set_bit(mm, kk);
+          const uint32_t uj = R[kRecJ], uk = R[kRecK];
+          const int64_t n = 32 * (int64_t)(w0 + (u & (S - 1))) + bit;
+          const int64_t node = ((int64_t)uk * d.M + uj) * L + n;
+          const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
+          const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
+          const long long shift = type == 0 ? shiftX : (type == 1 ? shiftY : shiftZ);
+          const long long row = rec_i64(R, kRecOff + 2 * type) +
+                                __popc(mm & ((1u << bit) - 1u)) + shift;
+          if (row < 0 || row >= A.points_cap) {
+            record_overflow(W.info);
+          } else {
+            const float t = interp_t(iso, s0, s1);
+            const float px = coord(x0, n, hx);
+            const float py = coord(y0, uj, hy);
+            const float pz = coord(z0, (int64_t)uk + A.k_offset, hz);
+            const float px1 = type == 0 ? coord(x0, n + 1, hx) : px;
+            const float py1 = type == 1 ? coord(y0, (int64_t)uj + 1, hy) : py;
+            const float pz1 = type == 2 ? coord(z0, (int64_t)uk + 1 + A.k_offset, hz) : pz;
+            float* o = A.points + row * 3;
+            o[0] = lerp_ref(px, px1, t);
+            o[1] = lerp_ref(py, py1, t);
+            o[2] = lerp_ref(pz, pz1, t);
+          }
+        }
+      }
+
+      // ---------------- phase 2b: triangles, lane = one active cell ----------------
+      for (unsigned e0 = 0; e0 < NC; e0 += 32) {
+        const unsigned e = e0 + lane;
+        const bool ve = e < NC;
+        int useg = -1;
+        unsigned nt = 0;
+        uint64_t pkc = 0;
+        const uint32_t* R = recs;
+        int cb = 0;
+        int64_t n = 0;
+        if (ve) {
+          const int u = find_word(recs, kRecCB, e);
+          R = recs + u * kRec;
+          useg = u >> logS;
+          cb = nth_set_bit(R[kRecAct], (int)(e - R[kRecCB]));
+          n = 32 * (int64_t)(w0 + (u & (S - 1))) + cb;
+          const int cs = cell_case(cb, R[kRecBits + 0], R[kRecBits + 1], R[kRecBits + 2],
+                                   R[kRecBits + 3], R[kRecBits + 4], R[kRecBits + 5],
+                                   R[kRecBits + 6], R[kRecBits + 7]);
+          pkc = s_case[cs];
+          nt = (unsigned)(pkc >> 60);
           if (nt && A.mask) {
-            const int64_t cell = (k * d.ny + j) * d.nx + 32 * (int64_t)w + b;
+            const int64_t cell = ((int64_t)R[kRecK] * d.ny + R[kRecJ]) * d.nx + n;
             if (__ldg(A.mask + cell) != 0) nt = 0;
           }
-          if (!nt) act &= ~(1u << b);
-          nt_lane += nt;
         }
-      }
-      // Segmented scans of the per-word counts, two 16-bit counts per lane.
-      const unsigned p0 = __popc(xa) | (__popc(ya) << 16);
-      const unsigned p1 = __popc(za) | (__popc(xb) << 16);
-      const unsigned p2 = __popc(xc) | (__popc(xd) << 16);
-      const unsigned p3 = __popc(yc) | (__popc(zb) << 16);
-      const unsigned i0 = seg_scan(p0, sl, S), i1 = seg_scan(p1, sl, S);
-      const unsigned i2 = seg_scan(p2, sl, S), i3 = seg_scan(p3, sl, S);
-      const unsigned i4 = seg_scan(nt_lane, sl, S);
-      const unsigned e0 = i0 - p0, e1 = i1 - p1, e2 = i2 - p2, e3 = i3 - p3, e4 = i4 - nt_lane;
-
-      const int64_t nbase = rowbit;  // node index of (0, j, k)
-      // ---- points of this node row: x, y, z sections ----
-      {
-        long long rel = oxa + cxa + (e0 & 0xffffu);
-        uint32_t m = xa;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          const int64_t i = 32 * (int64_t)w + b;
-          const float s = __ldg(A.v + nbase + i), s1 = __ldg(A.v + nbase + i + 1);
-          const float t = interp_t(iso, s, s1);
-          const float px = coord(x0, i, hx), px1 = coord(x0, i + 1, hx);
-          float* o = A.points + (outX + rel) * 3;
-          o[0] = lerp_ref(px, px1, t);
-          o[1] = lerp_ref(py, py, t);
-          o[2] = lerp_ref(pz, pz, t);
-          ++rel;
+        // Exclusive scan of nt within each run of lanes of one row.
+        unsigned incl = nt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
         }
-      }
-      {
-        long long rel = oya + cya + (e0 >> 16);
-        uint32_t m = ya;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          const int64_t i = 32 * (int64_t)w + b;
-          const float s = __ldg(A.v + nbase + i), s1 = __ldg(A.v + nbase + L + i);
-          const float t = interp_t(iso, s, s1);
-          const float px = coord(x0, i, hx);
-          float* o = A.points + (outY + rel) * 3;
-          o[0] = lerp_ref(px, px, t);
-          o[1] = lerp_ref(py, py1, t);
-          o[2] = lerp_ref(pz, pz, t);
-          ++rel;
+        const int prev_seg = __shfl_up_sync(0xffffffffu, useg, 1);
+        const bool head = lane == 0 || prev_seg != useg;
+        const uint32_t hm = __ballot_sync(0xffffffffu, head);
+        const int first = 31 - __clz(hm & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u)));
+        const unsigned before_run = __shfl_sync(0xffffffffu, incl, first > 0 ? first - 1 : 0);
+        const unsigned base_excl = first > 0 ? before_run : 0u;
+        const long long tbase = ve ? tri_cur[useg] : 0;
+        const bool last = lane == 31 || ((hm >> (lane + 1)) & 1u);
+        if (nt) {
+          const long long tpos = outT + tbase + (long long)(incl - nt - base_excl);
+          if (tpos < 0 || tpos + nt > A.conn_cap) {
+            record_overflow(W.info);
+          } else {
+            const uint32_t below = (1u << cb) - 1u;
+            const uint32_t below1 = cb == 31 ? 0xffffffffu : ((2u << cb) - 1u);
+            int32_t* o = A.conn + tpos * 3;
+            for (unsigned t = 0; t < 3 * nt; ++t) {
+              const unsigned ed = (unsigned)(pkc >> (4 * t)) & 0xfu;
+              const unsigned gp = (unsigned)(kEdgeGroup >> (4 * ed)) & 0xfu;
+              const unsigned g = gp & 7u;
+              const uint32_t lim = (gp & 8u) ? below1 : below;
+              o[t] = (int32_t)(rec_i64(R, kRecOff + 2 * g) + __popc(R[kRecMasks + g] & lim));
+            }
+          }
         }
+        __syncwarp();
+        if (ve && last) tri_cur[useg] = tbase + (long long)(incl - base_excl);
+        __syncwarp();
       }
-      {
-        long long rel = oza + cza + (e1 & 0xffffu);
-        uint32_t m = za;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          const int64_t i = 32 * (int64_t)w + b;
-          const float s = __ldg(A.v + nbase + i), s1 = __ldg(A.v + nbase + plane + i);
-          const float t = interp_t(iso, s, s1);
-          const float px = coord(x0, i, hx);
-          float* o = A.points + (outZ + rel) * 3;
-          o[0] = lerp_ref(px, px, t);
-          o[1] = lerp_ref(py, py, t);
-          o[2] = lerp_ref(pz, pz1, t);
-          ++rel;
-        }
-      }
-      // ---- triangles of this cell row ----
-      if (act) {
-        const long long Pxa = idX + oxa + cxa + (e0 & 0xffffu);
-        const long long Pya = idY + oya + cya + (e0 >> 16);
-        const long long Pza = idZ + oza + cza + (e1 & 0xffffu);
-        const long long Pxb = idX + oxb + cxb + (e1 >> 16);
-        const long long Pxc = idX + oxc + cxc + (e2 & 0xffffu);
-        const long long Pxd = idX + oxd + cxd + (e2 >> 16);
-        const long long Pyc = idY + oyc + cyc + (e3 & 0xffffu);
-        const long long Pzb = idZ + ozb + czb + (e3 >> 16);
-        long long tpos = outT + ota + ct + e4;
-        uint32_t m = act;
-        while (m) {
-          const int b = __ffs(m) - 1;
-          m &= m - 1;
-          const uint32_t lo = low_mask(b), lo1 = low_mask(b + 1);
-          s_pid[0][tid] = (int)(Pxa + __popc(xa & lo));
-          s_pid[1][tid] = (int)(Pya + __popc(ya & lo1));
-          s_pid[2][tid] = (int)(Pxb + __popc(xb & lo));
-          s_pid[3][tid] = (int)(Pya + __popc(ya & lo));
-          s_pid[4][tid] = (int)(Pxc + __popc(xc & lo));
-          s_pid[5][tid] = (int)(Pyc + __popc(yc & lo1));
-          s_pid[6][tid] = (int)(Pxd + __popc(xd & lo));
-          s_pid[7][tid] = (int)(Pyc + __popc(yc & lo));
-          s_pid[8][tid] = (int)(Pza + __popc(za & lo));
-          s_pid[9][tid] = (int)(Pza + __popc(za & lo1));
-          s_pid[10][tid] = (int)(Pzb + __popc(zb & lo));
-          s_pid[11][tid] = (int)(Pzb + __popc(zb & lo1));
-          const uint64_t pk = s_case[cell_case(b, q.a, a1, q.b, b1, q.c, c1, q.d, d1)];
-          const int nt = (int)(pk >> 60);
-          int32_t* o = A.conn + tpos * 3;
-          for (int t = 0; t < 3 * nt; ++t) o[t] = s_pid[(pk >> (4 * t)) & 0xfu][tid];
-          tpos += nt;
-        }
-      }
-      // Carry the segment totals to the next chunk of words.
-      const unsigned t0 = __shfl_sync(0xffffffffu, i0, S - 1, S);
-      const unsigned t1 = __shfl_sync(0xffffffffu, i1, S - 1, S);
-      const unsigned t2 = __shfl_sync(0xffffffffu, i2, S - 1, S);
-      const unsigned t3 = __shfl_sync(0xffffffffu, i3, S - 1, S);
-      const unsigned t4 = __shfl_sync(0xffffffffu, i4, S - 1, S);
-      cxa += t0 & 0xffffu; cya += t0 >> 16;
-      cza += t1 & 0xffffu; cxb += t1 >> 16;
-      cxc += t2 & 0xffffu; cxd += t2 >> 16;
-      cyc += t3 & 0xffffu; czb += t3 >> 16;
-      ct += t4;
+      __syncwarp();
     }
   }
 }
@@ -936,8 +1262,10 @@ k_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive, uint32_t* 
 
 struct FeLayout {
   FeDims d;
+  size_t k2_smem;  // dynamic shared memory of the count/scan kernel
   int64_t V, nwords, bits_stride;
-  size_t off_bits, off_rowoff, off_work, off_info, off_flags, off_agg, off_incl, total;
+  size_t off_bits, off_cnt, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
+      off_agg, off_incl, total;
   size_t reset_bytes;  // info + flags, zeroed before each scan
 };
 
@@ -960,7 +1288,20 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   while (S < d.W && S < 32) { S <<= 1; ++logS; }
   d.S = S;
   d.logS = logS;
-  d.ntiles = (d.R + kRowsPerTile - 1) / kRowsPerTile;
+  // K2: one thread per row up to 32 words per row; longer rows get 2^logP
+  // threads each (<= 32 words per thread while P <= 32).
+  int logP = 0;
+  while ((32 << logP) < d.W && logP < 5) ++logP;
+  const int64_t TR = kThreads >> logP;
+  d.TR = (int)TR;
+  d.logP = logP;
+  d.ctiles = (d.R + TR - 1) / TR;
+  d.ntiles = (d.R + kScanRows - 1) / kScanRows;
+  d.S3 = S < 8 ? S : 8;
+  d.logS3 = logS < 3 ? logS : 3;
+  const int64_t stage = (((TR + 1) * d.W + 3 + 8) + 3) & ~(int64_t)3;
+  f.k2_smem = (size_t)(2 * stage + 4 * TR) * 4;
+  if (f.k2_smem > 200 * 1024) return false;  // rows longer than ~90k nodes
   if (d.R > 0xffffffffLL) return false;  // worklist holds uint32 row ids
   f.V = d.L * d.M * d.N;
   f.nwords = (f.V + 31) / 32;
@@ -971,6 +1312,9 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.reset_bytes = o;
   f.off_agg = o;    o = align_up(o + (size_t)niso * d.ntiles * 4 * 8, 256);
   f.off_incl = o;   o = align_up(o + (size_t)niso * d.ntiles * 4 * 8, 256);
+  f.off_tot = o;    o = align_up(o + (size_t)niso * 4 * 8, 256);
+  f.off_base = o;   o = align_up(o + (size_t)niso * 8 * 8, 256);
+  f.off_cnt = o;    o = align_up(o + (size_t)niso * d.R * 4 * 4, 256);
   f.off_rowoff = o; o = align_up(o + (size_t)niso * d.R * 4 * 8, 256);
   f.off_work = o;   o = align_up(o + (size_t)niso * d.R * 4, 256);
   f.off_bits = o;   o = align_up(o + (size_t)niso * f.bits_stride * 4, 256);
@@ -986,6 +1330,8 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
     FeIsoWs& w = a.iso[q];
     w.bits = reinterpret_cast<uint32_t*>(b + f.off_bits) + (size_t)q * f.bits_stride;
     w.rowoff = reinterpret_cast<long long*>(b + f.off_rowoff) + (size_t)q * f.d.R * 4;
+    w.cnt = reinterpret_cast<int*>(b + f.off_cnt) + (size_t)q * f.d.R * 4;
+    w.tot = reinterpret_cast<long long*>(b + f.off_tot) + (size_t)q * 4;
     w.work = reinterpret_cast<uint32_t*>(b + f.off_work) + (size_t)q * f.d.R;
     w.flags = reinterpret_cast<uint32_t*>(b + f.off_flags) + (size_t)q * f.d.ntiles;
     w.agg = reinterpret_cast<long long*>(b + f.off_agg) + (size_t)q * f.d.ntiles * 4;
@@ -1162,8 +1508,14 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   TK_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + f.off_info, 0, f.reset_bytes - f.off_info, st));
   const int64_t skip = g_skip_tile.exchange(-1);
-  dim3 grid((unsigned)f.d.ntiles, (unsigned)niso);
-  k_fe_count_scan<<<grid, kThreads, 0, st>>>(f.d, v, mask, g_wait_ns.load(), skip);
+  if (f.k2_smem > 48 * 1024)
+    TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)f.k2_smem));
+  k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso), kThreads, f.k2_smem, st>>>(
+      f.d, v, mask, f.nwords);
+  TK_LAUNCHED();
+  k_fe_scan_rows<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
+      f.d, v, g_wait_ns.load(), skip);
   TK_LAUNCHED();
   return TKMC_OK;
 }
@@ -1204,6 +1556,27 @@ int tkmc_fe_row_offsets(int64_t nx, int64_t ny, int64_t nz, int niso, int iso,
   return TKMC_OK;
 }
 
+int tkmc_fe_check(int64_t nx, int64_t ny, int64_t nz, int niso, void* ws, size_t ws_bytes,
+                  void* stream) {
+  FeLayout f;
+  if (!fe_layout(nx, ny, nz, 0, niso, &f)) return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  int rc = check_ws(ws, ws_bytes, f.total);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  long long h[TKMC_MAX_ISO * 16];
+  TK_CUDA(cudaMemcpyAsync(h, static_cast<char*>(ws) + f.off_info, (size_t)niso * 16 * 8,
+                          cudaMemcpyDeviceToHost, st));
+  TK_CUDA(cudaStreamSynchronize(st));
+  for (int q = 0; q < niso; ++q) {
+    const long long e = h[q * 16 + 10];
+    if (e == TKMC_ERR_DEVICE_TIMEOUT)
+      return set_err((int)e, "fe scan look-back wait expired (isovalue %d)", q);
+    if (e)
+      return set_err((int)e, "fe emit wrote past the output capacity (isovalue %d)", q);
+  }
+  return TKMC_OK;
+}
+
 int tkmc_fe_count(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
                   const float* isovalues, int niso, const int32_t* mask, void* ws,
                   size_t ws_bytes, int64_t* counts, void* stream) {
@@ -1217,7 +1590,7 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
                  int64_t k_offset, const float* geom6, const float* isovalues, int niso,
                  const int32_t* mask, void* ws, size_t ws_bytes, const int64_t* pt_id_base,
                  const int64_t* pt_out_base, const int64_t* tri_out_base, float* points,
-                 int32_t* conn, void* stream) {
+                 int64_t points_capacity, int32_t* conn, int64_t conn_capacity, void* stream) {
   int rc = check_iso(isovalues, niso);
   if (rc) return rc;
   FeLayout f;
@@ -1231,6 +1604,8 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
   A.mask = mask;
   A.points = points;
   A.conn = conn;
+  A.points_cap = points ? points_capacity : 0;
+  A.conn_cap = conn ? conn_capacity : 0;
   for (int i = 0; i < 6; ++i) A.geom[i] = geom6[i];
   A.k_offset = k_offset;
   for (int q = 0; q < niso; ++q) {
@@ -1243,7 +1618,7 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
   }
   FeWsAll v = fe_views(f, ws, niso);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int G = 32 >> f.d.logS;
+  const int G = 32 >> f.d.logS3;
   const int g = grid_for(f.d.n_own_rows, (kThreads / 32) * G, 8);
   dim3 grid((unsigned)g, (unsigned)niso);
   k_fe_emit<<<grid, kThreads, 0, st>>>(f.d, v, A);
@@ -1278,8 +1653,10 @@ int tkmc_fe_run(const float* scalar, int64_t nx, int64_t ny, int64_t nz, const f
                    (long long)conn_capacity);
   if ((P > 0 && !points) || (T > 0 && !conn))
     return set_err(TKMC_ERR_INVALID_ARG, "output buffer is NULL");
-  return tkmc_fe_emit(scalar, nx, ny, nz, 0, 0, geom6, isovalues, niso, mask, ws, ws_bytes, id,
-                      id, tri, points, conn, stream);
+  rc = tkmc_fe_emit(scalar, nx, ny, nz, 0, 0, geom6, isovalues, niso, mask, ws, ws_bytes, id, id,
+                    tri, points, points_capacity, conn, conn_capacity, stream);
+  if (rc) return rc;
+  return tkmc_fe_check(nx, ny, nz, niso, ws, ws_bytes, stream);
 }
 
 int tkmc_mc_classify_cells(const float* scalar, int64_t nx, int64_t ny, int64_t nz,

@@ -87,7 +87,8 @@ def slab_bases(all_counts, rank):
 
 
 def _i64(vals):
-    return (ctypes.c_int64 * len(vals))(*[int(v) for v in np.asarray(vals).reshape(-1)])
+    flat = [int(v) for v in np.asarray(vals).reshape(-1)]
+    return (ctypes.c_int64 * len(flat))(*flat)
 
 
 def _f32(vals):
@@ -143,11 +144,18 @@ class SlabEngine:
                 local_values.data_ptr(), g.nx, g.ny, p.nz_cells, 1 if p.ghost else 0, p.k0,
                 _f32([g.x0, g.y0, g.z0, g.dx, g.dy, g.dz]), _f32(self.isos), len(self.isos),
                 None, self.ws.data_ptr(), self.nbytes, _i64(bases["id_base"]),
-                _i64(bases["out_base"]), _i64(bases["tri_out"]), pts.data_ptr(),
-                conn.data_ptr(), current_stream(self.dev)), "tkmc_fe_emit")
+                _i64(bases["out_base"]), _i64(bases["tri_out"]), pts.data_ptr(), own_p,
+                conn.data_ptr(), own_t, current_stream(self.dev)), "tkmc_fe_emit")
         return pts[:own_p * 3], conn[:own_t * 3]
 
-    def run(self, local_values):
+    def check(self):
+        """Synchronise and raise if the device recorded an error."""
+        g, p = self.grid, self.plan
+        _lib.check(self.lib.tkmc_fe_check(g.nx, g.ny, p.nz_cells, len(self.isos),
+                                          self.ws.data_ptr(), self.nbytes,
+                                          current_stream(self.dev)), "tkmc_fe_check")
+
+    def run(self, local_values, check=True):
         """count -> all-gather totals -> emit.  Returns this rank's slices."""
         counts = self.count(local_values)
         allc = self.exchange(counts)
@@ -156,6 +164,8 @@ class SlabEngine:
             raise OverflowError("global point total does not fit int32 point ids")
         b = slab_bases(allc, self.plan.rank)
         pts, conn = self.emit(local_values, counts, b)
+        if check:
+            self.check()
         return {"points_field": Field(f32, (pts.numel(),), CUDABuffer(pts)),
                 "conn_field": Field(i32, (conn.numel(),), CUDABuffer(conn)),
                 "counts": counts, "all_counts": allc, "bases": b,

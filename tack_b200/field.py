@@ -145,11 +145,15 @@ def from_torch(tensor, shape=None, writable=True):
 
 
 class _CudaArray:
-    """__cuda_array_interface__ view of external device memory."""
+    """__cuda_array_interface__ view of external device memory.
 
-    def __init__(self, ptr, n, dtype, readonly):
+    Always exported as writable (PyTorch rejects read-only interfaces);
+    read-only fields are enforced by Field._check_writable instead.
+    """
+
+    def __init__(self, ptr, n, dtype):
         self.__cuda_array_interface__ = {
-            "shape": (n,), "typestr": dtype.numpy_dtype.str, "data": (int(ptr), readonly),
+            "shape": (n,), "typestr": dtype.numpy_dtype.str, "data": (int(ptr), False),
             "version": 3, "strides": None,
         }
 
@@ -163,7 +167,7 @@ def field_from_ptr(ptr, dtype, shape, writable=False):
     if isinstance(shape, int):
         shape = (shape,)
     n = int(np.prod(shape, dtype=np.int64)) if len(shape) else 1
-    t = torch.as_tensor(_CudaArray(ptr, n, dtype, not writable), device=current_device())
+    t = torch.as_tensor(_CudaArray(ptr, n, dtype), device=current_device())
     return Field(dtype, shape, CUDABuffer(t), writable=writable)
 
 

@@ -68,7 +68,9 @@ def capi_fe(values, grid, isovalues, mask=None, want_rows=False):
     _lib.check(lib.tkmc_fe_emit(v.data_ptr(), nx, ny, nz, 0, 0, f32arr(grid[3:]),
                                 f32arr(isovalues), niso, m.data_ptr() if m is not None else None,
                                 ws.data_ptr(), nbytes, i64arr(ids), i64arr(ids), i64arr(tri),
-                                pts.data_ptr(), conn.data_ptr(), stream()), "tkmc_fe_emit")
+                                pts.data_ptr(), P, conn.data_ptr(), T, stream()), "tkmc_fe_emit")
+    _lib.check(lib.tkmc_fe_check(nx, ny, nz, niso, ws.data_ptr(), nbytes, stream()),
+               "tkmc_fe_check")
     torch.cuda.synchronize()
     return {"counts": counts.reshape(niso, 4), "points": pts[:P * 3].cpu().numpy().reshape(-1, 3),
             "conn": conn[:T * 3].cpu().numpy().reshape(-1, 3), "rows": rows,
@@ -88,13 +90,30 @@ def reference_offsets_from_rows(rows, counts, grid):
     return xo, yo, zo, r
 
 
+def assert_points_identical(a, b):
+    """Bit-identical f32 coordinates, NaN payloads aside.
+
+    A point on an edge with a NaN end is NaN on both sides, but the bits of
+    a NaN are not portable: x86 propagates the input NaN's payload
+    (0x7fc00000 for numpy's nan) while CUDA arithmetic returns the canonical
+    0x7fffffff.  NaN positions must match; every other coordinate must match
+    bit for bit.
+    """
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    assert a.shape == b.shape
+    na, nb = np.isnan(a), np.isnan(b)
+    np.testing.assert_array_equal(na, nb)
+    np.testing.assert_array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32))
+
+
 def assert_same_surface(got, ref, exact_points=True):
     """Counts and conn exact; points bit-identical (or within 1e-5 rel)."""
     assert got["total_points"] == ref["total_points"]
     assert got["total_tris"] == ref["total_tris"]
     np.testing.assert_array_equal(got["conn"], ref["conn"])
     if exact_points:
-        np.testing.assert_array_equal(got["points"].view(np.uint32), ref["points"].view(np.uint32))
+        assert_points_identical(got["points"], ref["points"])
     else:
         a, b = got["points"].astype(np.float64), ref["points"].astype(np.float64)
         np.testing.assert_array_less(np.abs(a - b), np.maximum(1e-5 * np.abs(b), 1e-5) + 1e-30)

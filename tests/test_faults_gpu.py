@@ -29,13 +29,13 @@ def short_wait():
 
 def test_fe_scan_wait_expires_with_status(tack, short_wait):
     lib = short_wait
-    c = load_fe_case("gyroid48")  # 48*48 node rows -> 9 tiles
+    c = load_fe_case("gyroid48")  # 48*48 node rows -> 3 scan tiles of 1024 rows
     nx, ny, nz = c["grid_tuple"][:3]
     v = torch.from_numpy(c["values"]).cuda()
     nb = lib.tkmc_fe_workspace_bytes(nx, ny, nz, 1)
     ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
     counts = np.zeros(4, np.int64)
-    lib.tkmc_test_skip_publish(3)
+    lib.tkmc_test_skip_publish(1)
     rc = lib.tkmc_fe_count(v.data_ptr(), nx, ny, nz, 0, f32arr([0.0]), 1, None, ws.data_ptr(), nb,
                            counts.ctypes.data, stream())
     assert rc == _lib.TKMC_ERR_DEVICE_TIMEOUT

@@ -11,7 +11,8 @@ import numpy as np
 import pytest
 
 from conftest import GOLDEN, golden_fe_cases, load_fe_case
-from fe_helpers import assert_same_surface, capi_fe, reference_offsets_from_rows
+from fe_helpers import (assert_points_identical, assert_same_surface, capi_fe,
+                        reference_offsets_from_rows)
 
 pytestmark = pytest.mark.gpu
 
@@ -39,7 +40,7 @@ def test_api_matches_reference(tack, name):
     assert_same_surface(r, ref)
     assert r["block_point_counts"] == [ref["total_points"]]
     assert r["block_tri_counts"] == [ref["total_tris"]]
-    np.testing.assert_array_equal(r["points_field"].to_numpy().reshape(-1, 3), r["points"])
+    assert_points_identical(r["points_field"].to_numpy().reshape(-1, 3), r["points"])
     np.testing.assert_array_equal(r["conn_field"].to_numpy().reshape(-1, 3), r["conn"])
 
 
@@ -71,7 +72,7 @@ def test_multiblock_matches_reference(tack):
         blocks.append({"scalar": _upload(tack, z[f"values{b}"], tack.f32), "grid": grid})
     r = tack.flying_edges_multiblock(blocks, 0.0)
     np.testing.assert_array_equal(r["conn"], z["conn"])
-    np.testing.assert_array_equal(r["points"].view(np.uint32), z["points"].view(np.uint32))
+    assert_points_identical(r["points"], z["points"])
     assert r["block_point_counts"] == list(z["block_point_counts"])
     assert r["block_tri_counts"] == list(z["block_tri_counts"])
 
@@ -136,8 +137,7 @@ def test_fe_run_capacity_protocol(tack):
                          counts.ctypes.data, stream())
     assert rc == 0
     np.testing.assert_array_equal(conn.cpu().numpy().reshape(-1, 3), c["conn"])
-    np.testing.assert_array_equal(pts.cpu().numpy().reshape(-1, 3).view(np.uint32),
-                                  c["points"].view(np.uint32))
+    assert_points_identical(pts.cpu().numpy().reshape(-1, 3), c["points"])
     del ctypes
 
 
