@@ -365,6 +365,7 @@ struct FeDims {
   int64_t ntiles;       // K2b scan tiles
   int64_t ctiles;       // K2a count tiles
   int W;                // 32-bit words per row
+  int AW;               // words of the per-row activity mask = ceil(W / 32)
   int S, logS;          // lanes per row (power of two <= 32)
   int TR;               // K2 tile height in rows
   int logP;             // K2 threads per row = 1 << logP (TR << logP == block size)
@@ -375,6 +376,7 @@ struct FeDims {
 struct FeIsoWs {
   uint32_t* bits;       // flat node bitmask
   int* cnt;             // [R][4] row counts X, Y, Z, T
+  uint32_t* wact;       // [R][AW] words of each row with any output (bitmask)
   long long* tot;       // [4] this slab's own totals (contiguous across isovalues)
   long long* rowoff;    // [R][4] exclusive offsets X, Y, Z, T (section-relative)
   uint32_t* work;       // active own rows
@@ -438,36 +440,49 @@ __device__ __forceinline__ uint32_t active_cells(const Quad& q, uint32_t xcell_m
 }
 
 // ------------------------------------------------------------------------
-// K2: per-row counts + single-pass scan + worklist
+// K2: per-row counts (K2a), then a single-pass scan of them (K2b)
 // ------------------------------------------------------------------------
+
+// Triangles of the (up to 32) cells of one word, bit-parallel.  For every
+// case of the marching-cubes table, triangles = V - 2F - 4*belt + 4*full,
+// where V counts corners above the isovalue, F the faces with all four
+// corners above, belt is 1 when exactly two antipodal corners are below, and
+// full is 1 when all eight are above.  (It is #cut edges - 2 * #components
+// of the above corners, with the cube graph's two kinds of non-face cycles
+// corrected; checked against all 256 table entries.)  Corner words:
+// 0 a, 1 a1, 2 b1, 3 b, 4 c, 5 c1, 6 d1, 7 d; xm selects the valid cells.
+__device__ __forceinline__ unsigned tri_count_word(uint32_t a, uint32_t a1, uint32_t b,
+                                                   uint32_t b1, uint32_t c, uint32_t c1,
+                                                   uint32_t d, uint32_t d1, uint32_t xm) {
+  const unsigned V = __popc(a & xm) + __popc(a1 & xm) + __popc(b & xm) + __popc(b1 & xm) +
+                     __popc(c & xm) + __popc(c1 & xm) + __popc(d & xm) + __popc(d1 & xm);
+  const uint32_t ab = a & b, a1b1 = a1 & b1, cd = c & d, c1d1 = c1 & d1;
+  const uint32_t f0 = ab & a1b1;        // corners 0 1 2 3
+  const uint32_t f1 = cd & c1d1;        // 4 5 6 7
+  const uint32_t f2 = a & a1 & c & c1;  // 0 1 5 4
+  const uint32_t f3 = b & b1 & d & d1;  // 3 2 6 7
+  const uint32_t f4 = ab & cd;          // 0 3 7 4
+  const uint32_t f5 = a1b1 & c1d1;      // 1 2 6 5
+  const unsigned F = __popc(f0 & xm) + __popc(f1 & xm) + __popc(f2 & xm) + __popc(f3 & xm) +
+                     __popc(f4 & xm) + __popc(f5 & xm);
+  const uint32_t full = f0 & f1 & xm;
+  const uint32_t belt = (~a & ~d1 & a1 & b1 & b & c & c1 & d) |   // 0 and 6 below
+                        (~a1 & ~d & a & b1 & b & c & c1 & d1) |   // 1 and 7
+                        (~b1 & ~c & a & a1 & b & c1 & d1 & d) |   // 2 and 4
+                        (~b & ~c1 & a & a1 & b1 & c & d1 & d);    // 3 and 5
+  return V - 2 * F - 4 * __popc(belt & xm) + 4 * __popc(full);
+}
+
+// K2a: per-row counts {X, Y, Z, T} of one tile of TR rows -> cnt[R][4],
+// and per-row word-activity masks -> wact[R][AW].  Tiles are independent.
 //
-// A tile is TR consecutive node rows (linear order r = k*M + j).  Its bit
-// rows [R0, R0+TR] and their next-plane neighbours [R0+M, R0+M+TR] are
-// staged in shared memory with coalesced loads (each is one contiguous run
-// of the flat bitmask), so the counting touches no global memory.  Rows are
-// handled by S-lane segments (S words per pass); per-row totals are reduced
-// in the segment, scanned across the tile, and chained across tiles by the
-// decoupled look-back.
-
-// Word w of the row whose first node sits at bit rb of the staged run s.
-__device__ __forceinline__ uint32_t sm_row_word(const uint32_t* s, int64_t rb, int w,
-                                                int64_t L) {
-  const int64_t rem = L - 32 * (int64_t)w;
-  if (rem <= 0) return 0u;
-  const int64_t pos = rb + 32 * (int64_t)w;
-  const int64_t q = pos >> 5;
-  const int sh = (int)(pos & 31);
-  uint32_t x = s[q];
-  if (sh) x = __funnelshift_r(x, s[q + 1], sh);
-  if (rem < 32) x &= (1u << rem) - 1u;
-  return x;
-}
-
-// Words reserved per staged run: the run itself, the 16-byte alignment
-// shift in front of it and the rounding of the last 16-byte copy.
-__device__ __forceinline__ int64_t k2_stage_words(const FeDims& d) {
-  return (((int64_t)(d.TR + 1) * d.W + 3 + 8) + 3) & ~(int64_t)3;
-}
+// The tile's bit rows [R0, R0+TR] and their next-plane neighbours
+// [R0+M, R0+M+TR] are each one contiguous run of the flat bitmask; both are
+// copied to shared memory with 16-byte cp.async (all copies in flight at
+// once).  A row is then handled by an S-lane segment, one word per lane
+// (S = 32 for rows of >= 1024 nodes, fewer for short rows, which then share
+// a warp).  Warps whose rows have no side change anywhere skip the word
+// arithmetic entirely; the surface is sparse, so most rows do.
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
@@ -509,112 +524,139 @@ __device__ __forceinline__ uint32_t staged_word(const uint32_t* s, int b, int w,
   return x;
 }
 
-// Triangles of the (up to 32) cells of one word, bit-parallel.  For every
-// case of the marching-cubes table, triangles = V - 2F - 4*belt + 4*full,
-// where V counts corners above the isovalue, F the faces with all four
-// corners above, belt is 1 when exactly two antipodal corners are below, and
-// full is 1 when all eight are above.  (It is #cut edges - 2 * #components
-// of the above corners, with the cube graph's two kinds of non-face cycles
-// corrected; checked against all 256 table entries.)  Corner words:
-// 0 a, 1 a1, 2 b1, 3 b, 4 c, 5 c1, 6 d1, 7 d; xm selects the valid cells.
-__device__ __forceinline__ unsigned tri_count_word(uint32_t a, uint32_t a1, uint32_t b,
-                                                   uint32_t b1, uint32_t c, uint32_t c1,
-                                                   uint32_t d, uint32_t d1, uint32_t xm) {
-  const unsigned V = __popc(a & xm) + __popc(a1 & xm) + __popc(b & xm) + __popc(b1 & xm) +
-                     __popc(c & xm) + __popc(c1 & xm) + __popc(d & xm) + __popc(d1 & xm);
-  const uint32_t ab = a & b, a1b1 = a1 & b1, cd = c & d, c1d1 = c1 & d1;
-  const uint32_t f0 = ab & a1b1;        // corners 0 1 2 3
-  const uint32_t f1 = cd & c1d1;        // 4 5 6 7
-  const uint32_t f2 = a & a1 & c & c1;  // 0 1 5 4
-  const uint32_t f3 = b & b1 & d & d1;  // 3 2 6 7
-  const uint32_t f4 = ab & cd;          // 0 3 7 4
-  const uint32_t f5 = a1b1 & c1d1;      // 1 2 6 5
-  const unsigned F = __popc(f0 & xm) + __popc(f1 & xm) + __popc(f2 & xm) + __popc(f3 & xm) +
-                     __popc(f4 & xm) + __popc(f5 & xm);
-  const uint32_t full = f0 & f1 & xm;
-  const uint32_t belt = (~a & ~d1 & a1 & b1 & b & c & c1 & d) |   // 0 and 6 below
-                        (~a1 & ~d & a & b1 & b & c & c1 & d1) |   // 1 and 7
-                        (~b1 & ~c & a & a1 & b & c1 & d1 & d) |   // 2 and 4
-                        (~b & ~c1 & a & a1 & b1 & c & d1 & d);    // 3 and 5
-  return V - 2 * F - 4 * __popc(belt & xm) + 4 * __popc(full);
+// Words per staged run: the run, the 16-byte alignment shift in front of it
+// and the rounding of the last 16-byte copy.
+__host__ __device__ __forceinline__ int64_t k2_stage_words(int TR, int W) {
+  return (((int64_t)(TR + 1) * W + 3 + 8) + 3) & ~(int64_t)3;
 }
 
-// Counts of one row over words [wbeg, wbeg + WP) visited from word wbeg + rot
-// (rotation keeps the threads of a warp on different banks).  ALIGNED: the
-// row length is a multiple of 32 nodes, so every row starts on a word.
+// Rows of one K2a tile, ALIGNED = every row starts on a word (L % 32 == 0).
 template <bool ALIGNED>
-__device__ __forceinline__ void count_row_words(
-    const uint32_t* sAr, const uint32_t* sCr, int ba, int bb, int bc, int bd, int Li, int W,
-    int wbeg, int WP, int rot, bool hasY, bool hasZ, const int* s_ntri,
-    const int32_t* __restrict__ mask, int64_t cell_row0, unsigned& cX, unsigned& cY,
-    unsigned& cZ, unsigned& cT) {
-  const bool hasC = hasY && hasZ;
-  int wl = rot;
-#pragma unroll 4
-  for (int i = 0; i < WP; ++i) {
-    const int w = wbeg + wl;
-    wl = (wl + 1 == WP) ? 0 : wl + 1;
-    if (w >= W) continue;
-    uint32_t a, an, b = 0, bn = 0, c = 0, cn = 0, dd = 0, dn = 0;
-    if (ALIGNED) {
-      const bool more = w + 1 < W;
-      const int qa = (ba >> 5) + w;
-      a = sAr[qa];
-      an = more ? (sAr[qa + 1] & 1u) : 0u;
-      if (hasY) { const int q = (bb >> 5) + w; b = sAr[q]; bn = more ? (sAr[q + 1] & 1u) : 0u; }
-      if (hasZ) { const int q = (bc >> 5) + w; c = sCr[q]; cn = more ? (sCr[q + 1] & 1u) : 0u; }
-      if (hasC) { const int q = (bd >> 5) + w; dd = sCr[q]; dn = more ? (sCr[q + 1] & 1u) : 0u; }
-    } else {
-      a = staged_word(sAr, ba, w, Li, &an);
-      if (hasY) b = staged_word(sAr, bb, w, Li, &bn);
-      if (hasZ) c = staged_word(sCr, bc, w, Li, &cn);
-      if (hasC) dd = staged_word(sCr, bd, w, Li, &dn);
+__device__ __forceinline__ void count_rows(const FeDims& d, const FeIsoWs& Wk,
+                                           const int32_t* __restrict__ mask, const int* s_ntri,
+                                           const uint32_t* sAr, const uint32_t* sCr,
+                                           int64_t R0, int64_t a_first, int64_t c_first) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int S = d.S, logS = d.logS, G = 32 >> logS;
+  const int seg = lane >> logS, sl = lane & (S - 1);
+  const int W = d.W, TR = d.TR;
+  const int64_t L = d.L;
+  const int Li = (int)L;
+  const uint32_t M32 = (uint32_t)d.M;
+  const int passes = (TR + 8 * G - 1) / (8 * G);
+  // Row of pass 0, then advance by 8G rows per pass without dividing.
+  const int local0 = warp * G + seg;
+  uint32_t j = (uint32_t)(R0 + local0) % M32, k = (uint32_t)(R0 + local0) / M32;
+  const uint32_t step = 8u * (uint32_t)G, dj = step % M32, dk = step / M32;
+  for (int p = 0; p < passes; ++p) {
+    const int local = local0 + p * (int)step;
+    if (p > 0) {
+      j += dj;
+      k += dk;
+      if (j >= M32) { j -= M32; ++k; }
     }
-    const uint32_t xm = low_mask(Li - 1 - 32 * w);
-    const uint32_t a1 = (a >> 1) | (an << 31);
-    cX += __popc((a ^ a1) & xm);
-    if (hasY) cY += __popc(a ^ b);
-    if (hasZ) cZ += __popc(a ^ c);
-    if (hasC) {
-      const uint32_t b1 = (b >> 1) | (bn << 31), c1 = (c >> 1) | (cn << 31);
-      const uint32_t d1 = (dd >> 1) | (dn << 31);
-      cT += tri_count_word(a, a1, b, b1, c, c1, dd, d1, xm);
-      if (mask) {  // masked cells emit nothing: take their triangles back out
-        const uint32_t u = (a ^ b) | (a ^ c) | (a ^ dd);
-        const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
-        uint32_t act = (u | (u >> 1) | (un << 31) | (a ^ a1)) & xm;
-        while (act) {
-          const int bit = __ffs(act) - 1;
-          act &= act - 1;
-          if (__ldg(mask + cell_row0 + 32 * w + bit) != 0)
-            cT -= s_ntri[cell_case(bit, a, a1, b, b1, c, c1, dd, d1)];
+    const int64_t r = R0 + local;
+    const bool valid = local < TR && r < d.R;
+    const bool hasY = valid && (j + 1 < M32);
+    const bool hasZ = valid && ((int64_t)k + 1 < d.N);
+    const bool hasC = hasY && hasZ;
+    const int ba = (int)(r * L - a_first * 32), bb = ba + Li;
+    const int bc = (int)((r + d.M) * L - c_first * 32), bd = bc + Li;
+    unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
+    bool any = false;
+    for (int w0 = 0; w0 < W; w0 += S) {
+      const int w = w0 + sl;
+      uint32_t a = 0, an = 0, b, bn, c, cn, dd, dn;
+      if (ALIGNED) {
+        const bool in = w < W, more = w + 1 < W;
+        if (valid && in) { a = sAr[(ba >> 5) + w]; an = more ? (sAr[(ba >> 5) + w + 1] & 1u) : 0u; }
+        if (hasY && in) { b = sAr[(bb >> 5) + w]; bn = more ? (sAr[(bb >> 5) + w + 1] & 1u) : 0u; }
+        else { b = a; bn = an; }
+        if (hasZ && in) { c = sCr[(bc >> 5) + w]; cn = more ? (sCr[(bc >> 5) + w + 1] & 1u) : 0u; }
+        else { c = a; cn = an; }
+        if (hasC && in) { dd = sCr[(bd >> 5) + w]; dn = more ? (sCr[(bd >> 5) + w + 1] & 1u) : 0u; }
+        else { dd = b; dn = bn; }
+      } else {
+        if (valid) a = staged_word(sAr, ba, w, Li, &an);
+        // A missing neighbour row reads as a copy of row a (no crossings).
+        if (hasY) b = staged_word(sAr, bb, w, Li, &bn); else { b = a; bn = an; }
+        if (hasZ) c = staged_word(sCr, bc, w, Li, &cn); else { c = a; cn = an; }
+        if (hasC) dd = staged_word(sCr, bd, w, Li, &dn); else { dd = b; dn = bn; }
+      }
+      const uint32_t a1 = (a >> 1) | (an << 31);
+      const uint32_t u = (a ^ b) | (a ^ c) | (a ^ dd);
+      const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
+      const bool busy = ((u | (a ^ a1) | (un << 31)) & low_mask(Li - 32 * w)) != 0u;
+      // Warps with no side change in any of their rows skip the arithmetic.
+      const uint32_t bal = __ballot_sync(0xffffffffu, busy);
+      uint32_t amask = 0;
+      if (bal != 0u) {
+        any = true;
+        unsigned x0 = 0, y0 = 0, z0 = 0, t0 = 0;
+        if (busy) {
+          const uint32_t xm = low_mask(Li - 1 - 32 * w);
+          x0 = __popc((a ^ a1) & xm);
+          y0 = __popc(a ^ b);
+          z0 = __popc(a ^ c);
+          if (hasC) {
+            const uint32_t b1 = (b >> 1) | (bn << 31), c1 = (c >> 1) | (cn << 31);
+            const uint32_t d1 = (dd >> 1) | (dn << 31);
+            t0 = tri_count_word(a, a1, b, b1, c, c1, dd, d1, xm);
+            if (mask) {  // masked cells emit nothing: take their triangles back out
+              const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
+              uint32_t act = (u | (u >> 1) | (un << 31) | (a ^ a1)) & xm;
+              while (act) {
+                const int bit = __ffs(act) - 1;
+                act &= act - 1;
+                if (__ldg(mask + cell_row0 + 32 * w + bit) != 0)
+                  t0 -= s_ntri[cell_case(bit, a, a1, b, b1, c, c1, dd, d1)];
+              }
+            }
+          }
+          cX += x0;
+          cY += y0;
+          cZ += z0;
+          cT += t0;
         }
+        // Activity bits of words [w0, w0 + S) of this segment's row.  Either
+        // the row fits one segment (w0 == 0) or S == 32, so each chunk owns
+        // exactly one mask word.
+        amask = (__ballot_sync(0xffffffffu, (x0 | y0 | z0 | t0) != 0u) >> (seg << logS)) &
+                low_mask(S);
+      }
+      if (sl == 0 && valid) Wk.wact[r * d.AW + (w0 >> 5)] = amask;
+    }
+    if (any) {  // row totals over the segment (all zero otherwise)
+      for (int o = S >> 1; o > 0; o >>= 1) {
+        cX += __shfl_xor_sync(0xffffffffu, cX, o);
+        cY += __shfl_xor_sync(0xffffffffu, cY, o);
+        cZ += __shfl_xor_sync(0xffffffffu, cZ, o);
+        cT += __shfl_xor_sync(0xffffffffu, cT, o);
       }
     }
+    if (sl == 0 && valid)
+      reinterpret_cast<int4*>(Wk.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
   }
 }
 
-// K2a: per-row counts {X, Y, Z, T} of one tile of TR rows -> cnt[R][4].
-// Tiles are independent (no inter-tile waits).
 __global__ void __launch_bounds__(kThreads, 3)
 k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nwords) {
   extern __shared__ uint32_t k2_smem[];
   __shared__ int s_ntri[256];
-  const FeIsoWs& W = ws.iso[blockIdx.y];
+  const FeIsoWs& Wk = ws.iso[blockIdx.y];
   const int tid = threadIdx.x;
-  const int64_t stage = k2_stage_words(d);
+  const int TR = d.TR, W = d.W;
+  const int64_t stage = k2_stage_words(TR, W);
   uint32_t* sA = k2_smem;
   uint32_t* sC = k2_smem + stage;
   s_ntri[tid] = (int)(c_case_tris[tid] >> 60);
-  const int TR = d.TR;
   const int64_t R0 = (int64_t)blockIdx.x * TR;
   const int64_t L = d.L;
 
-  // Stage the two runs of bit rows (all copies in flight at once).
   const int64_t a_first = (R0 * L) >> 5;
   const int64_t a_last_row = min(R0 + TR + 1, d.R);
   const int64_t a_words = min(((a_last_row * L + 31) >> 5) + 1, nwords + 1) - a_first;
-  const uint32_t* sAr = sA + stage_run(sA, W.bits, a_first, a_words);
+  const uint32_t* sAr = sA + stage_run(sA, Wk.bits, a_first, a_words);
   const int64_t c_row0 = R0 + d.M;
   int64_t c_first = 0;
   const uint32_t* sCr = sC;
@@ -622,43 +664,14 @@ k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nword
     c_first = (c_row0 * L) >> 5;
     const int64_t c_last_row = min(c_row0 + TR + 1, d.R);
     const int64_t c_words = min(((c_last_row * L + 31) >> 5) + 1, nwords + 1) - c_first;
-    sCr = sC + stage_run(sC, W.bits, c_first, c_words);
+    sCr = sC + stage_run(sC, Wk.bits, c_first, c_words);
   }
   cp_async_wait_all();
   __syncthreads();
-
-  // Thread (row, part): P threads per row, each over a contiguous share of
-  // the row's words.
-  const int P = 1 << d.logP;
-  const int row_local = tid >> d.logP, part = tid & (P - 1);
-  const int64_t r = R0 + row_local;
-  const bool valid = r < d.R;
-  const uint32_t r32 = (uint32_t)r, M32 = (uint32_t)d.M;
-  const uint32_t j = valid ? r32 % M32 : 0u, k = valid ? r32 / M32 : 0u;
-  const bool hasY = valid && (j + 1 < M32);
-  const bool hasZ = valid && ((int64_t)k + 1 < d.N);
-  const int Li = (int)L;
-  const int ba = (int)(r * L - a_first * 32), bb = ba + Li;
-  const int bc = (int)((r + d.M) * L - c_first * 32), bd = bc + Li;
-  unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
-  if (valid) {
-    const int WP = (d.W + P - 1) >> d.logP;
-    const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
-    if ((L & 31) == 0)
-      count_row_words<true>(sAr, sCr, ba, bb, bc, bd, Li, d.W, part * WP, WP, row_local % WP,
-                            hasY, hasZ, s_ntri, mask, cell_row0, cX, cY, cZ, cT);
-    else
-      count_row_words<false>(sAr, sCr, ba, bb, bc, bd, Li, d.W, part * WP, WP, row_local % WP,
-                             hasY, hasZ, s_ntri, mask, cell_row0, cX, cY, cZ, cT);
-  }
-  for (int o = P >> 1; o > 0; o >>= 1) {
-    cX += __shfl_xor_sync(0xffffffffu, cX, o);
-    cY += __shfl_xor_sync(0xffffffffu, cY, o);
-    cZ += __shfl_xor_sync(0xffffffffu, cZ, o);
-    cT += __shfl_xor_sync(0xffffffffu, cT, o);
-  }
-  if (part == 0 && valid)
-    reinterpret_cast<int4*>(W.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
+  if ((L & 31) == 0)
+    count_rows<true>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
+  else
+    count_rows<false>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
 }
 
 // K2b: single-pass (decoupled look-back) exclusive scan of the row counts
@@ -866,7 +879,7 @@ __device__ __forceinline__ int find_word(const uint32_t* recs, int field, unsign
 }
 
 __global__ void __launch_bounds__(kThreads, 3)
-k_fe_emit(FeDims d, FeWsAll ws, FeEmitArgs A) {
+k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
   __shared__ uint32_t s_rec[kThreads / 32][32 * kRec];
   __shared__ long long s_tri[kThreads / 32][32];  // running triangle offset per row segment
@@ -1099,6 +1112,407 @@ k_fe_emit(FeDims d, FeWsAll ws, FeEmitArgs A) {
 }
 
 // ------------------------------------------------------------------------
+// K3 (words): emit with work proportional to the active words
+// ------------------------------------------------------------------------
+//
+// A warp takes up to 32 active rows at a time.  For each row, the union of
+// the word-activity masks of the four node rows around it (row, +y, +z,
+// +y+z) marks every word where any of its eight point-id sequences or its
+// triangle sequence advances; all other words contribute nothing.  Those
+// words ("units") of all 32 rows are packed into batches of 32 lanes:
+//   1. lane = unit: load the unit's four bit words, form the crossing masks
+//      and the unit's triangle count, and scan them per row (segmented) into
+//      absolute offsets;
+//   2. lane = one crossing of the batch: emit the point;
+//   3. lane = one active cell of the batch: emit its triangles.
+
+constexpr int kMaxAW = 8;  // rows up to 8192 nodes take this kernel
+
+// Unit record (32-bit words, odd stride).
+constexpr int kUR = 39;
+constexpr int kURMask = 0;   // 8 crossing masks
+constexpr int kURAct = 8;    // cells with triangles
+constexpr int kURBits = 9;   // a a1 b b1 c c1 d d1
+constexpr int kUROff = 17;   // 8 x int64 id offsets at the unit's first node
+constexpr int kURTri = 33;   // int64 triangle offset of the unit's first cell
+constexpr int kURSlot = 35;  // row slot in the warp
+constexpr int kURW = 36;     // word index in the row
+constexpr int kURPB = 37;    // exclusive prefix of points over the batch
+constexpr int kURCB = 38;    // exclusive prefix of active cells over the batch
+// Row slot record (32-bit words).
+constexpr int kSR = 21;
+constexpr int kSROff = 0;    // 8 x int64 running id offsets
+constexpr int kSRTri = 16;   // int64 running triangle offset
+constexpr int kSRJ = 18, kSRK = 19, kSRUB = 20;  // j, k, first unit of the row
+
+struct EmitSmem {
+  uint32_t unit[kThreads / 32][32 * kUR];
+  uint32_t slot[kThreads / 32][32 * kSR + 1];
+  uint32_t umask[kThreads / 32][32 * kMaxAW];
+};
+
+// Position of the k-th set bit across the AW words of m (k < total popcount).
+__device__ __forceinline__ int nth_set_bit_multi(const uint32_t* m, int AW, int k) {
+  for (int i = 0; i < AW; ++i) {
+    const int c = __popc(m[i]);
+    if (k < c) return 32 * i + nth_set_bit(m[i], k);
+    k -= c;
+  }
+  return -1;
+}
+
+// Largest slot s with rec[s * stride + field] <= e (field non-decreasing).
+__device__ __forceinline__ int find_slot(const uint32_t* base, int stride, int field,
+                                         unsigned e) {
+  int lo = 0;
+#pragma unroll
+  for (int step = 16; step >= 1; step >>= 1) {
+    const int m = lo + step;
+    if (m < 32 && base[m * stride + field] <= e) lo = m;
+  }
+  return lo;
+}
+
+// Exclusive prefix of `x` over the lanes of the caller's run, where runs are
+// maximal sequences of lanes with equal `key` (keys of a run are contiguous).
+// *run_total receives the run's total in the run's last lane.
+__device__ __forceinline__ unsigned seg_excl(unsigned x, int key, unsigned* run_total,
+                                             bool* is_last) {
+  const int lane = threadIdx.x & 31;
+  unsigned incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int prev = __shfl_up_sync(0xffffffffu, key, 1);
+  const bool head = lane == 0 || prev != key;
+  const uint32_t hm = __ballot_sync(0xffffffffu, head);
+  const int first = 31 - __clz(hm & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u)));
+  const unsigned before = __shfl_sync(0xffffffffu, incl, first > 0 ? first - 1 : 0);
+  const unsigned base = first > 0 ? before : 0u;
+  *is_last = lane == 31 || ((hm >> (lane + 1)) & 1u);
+  *run_total = incl - base;
+  return incl - x - base;
+}
+
+__device__ __forceinline__ long long ld_i64(const uint32_t* p) {
+  return (long long)(((unsigned long long)p[1] << 32) | p[0]);
+}
+__device__ __forceinline__ void st_i64(uint32_t* p, long long v) {
+  p[0] = (uint32_t)(unsigned long long)v;
+  p[1] = (uint32_t)((unsigned long long)v >> 32);
+}
+
+// Word w of a row (first node at flat bit rowbit) and bit 0 of word w + 1.
+__device__ __forceinline__ uint32_t row_word_next(const uint32_t* __restrict__ bits,
+                                                  int64_t rowbit, int w, int64_t L,
+                                                  uint32_t* next0) {
+  const int64_t rem = L - 32 * (int64_t)w;
+  if (rem <= 0) {
+    *next0 = 0u;
+    return 0u;
+  }
+  const int64_t pos = rowbit + 32 * (int64_t)w;
+  const int64_t q = pos >> 5;
+  const int sh = (int)(pos & 31);
+  const uint32_t lo = __ldg(bits + q), hi = __ldg(bits + q + 1);
+  uint32_t x = sh ? __funnelshift_r(lo, hi, sh) : lo;
+  uint32_t nx0 = 0u;
+  if (rem > 32) nx0 = sh ? (hi >> sh) & 1u : (hi & 1u);
+  *next0 = nx0;
+  if (rem < 32) x &= (1u << rem) - 1u;
+  return x;
+}
+
+__global__ void __launch_bounds__(kThreads, 3)
+k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
+  extern __shared__ uint32_t k3_smem[];
+  __shared__ uint64_t s_case[256];
+  EmitSmem& S = *reinterpret_cast<EmitSmem*>(k3_smem);
+  const int isoi = blockIdx.y;
+  const FeIsoWs& W = ws.iso[isoi];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_case[tid] = c_case_tris[tid];
+  __syncthreads();
+  uint32_t* U = S.unit[warp];
+  uint32_t* SL = S.slot[warp];
+  uint32_t* UM = S.umask[warp];
+  const int AW = d.AW;
+  const int64_t L = d.L, plane = d.L * d.M;
+  const uint32_t M32 = (uint32_t)d.M;
+  const int64_t n_active = *((volatile long long*)(W.info + 8));
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const float iso = A.iso.v[isoi];
+  const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
+  const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
+  const long long idX = A.pt_id_base[isoi][0], idY = A.pt_id_base[isoi][1],
+                  idZ = A.pt_id_base[isoi][2];
+  const long long shiftX = A.pt_out_base[isoi][0] - idX;
+  const long long shiftY = A.pt_out_base[isoi][1] - idY;
+  const long long shiftZ = A.pt_out_base[isoi][2] - idZ;
+  const long long outT = A.tri_out_base[isoi];
+
+  for (int64_t grp = gw; grp * 32 < n_active; grp += nw) {
+    // ---- rows: lane = one active row ----
+    const int64_t item = grp * 32 + lane;
+    const bool valid = item < n_active;
+    const int64_t r = valid ? (int64_t)W.work[item] : 0;
+    const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
+    const bool hasY = valid && (j + 1 < M32);
+    const bool hasZ = valid && ((int64_t)k + 1 < d.N);
+    const bool hasC = hasY && hasZ;
+    long long off[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    long long ota = 0;
+    unsigned nu = 0;
+    uint32_t* um = UM + lane * kMaxAW;
+    for (int i = 0; i < AW; ++i) {
+      uint32_t m = 0;
+      if (valid) m = __ldg(W.wact + r * AW + i);
+      if (hasY) m |= __ldg(W.wact + (r + 1) * AW + i);
+      if (hasZ) m |= __ldg(W.wact + (r + d.M) * AW + i);
+      if (hasC) m |= __ldg(W.wact + (r + d.M + 1) * AW + i);
+      um[i] = m;
+      nu += __popc(m);
+    }
+    if (valid) {
+      const longlong2* ra = reinterpret_cast<const longlong2*>(W.rowoff + r * 4);
+      const longlong2 p0 = ra[0], p1 = ra[1];
+      off[0] = p0.x + idX;
+      off[1] = p0.y + idY;
+      off[2] = p1.x + idZ;
+      ota = p1.y;
+    }
+    if (hasY) {
+      off[3] = W.rowoff[(r + 1) * 4 + 0] + idX;
+      off[7] = W.rowoff[(r + 1) * 4 + 2] + idZ;
+    }
+    if (hasZ) {
+      off[4] = W.rowoff[(r + d.M) * 4 + 0] + idX;
+      off[6] = W.rowoff[(r + d.M) * 4 + 1] + idY;
+    }
+    if (hasC) off[5] = W.rowoff[(r + d.M + 1) * 4 + 0] + idX;
+    uint32_t* sl = SL + lane * kSR;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) st_i64(sl + kSROff + 2 * g, off[g]);
+    st_i64(sl + kSRTri, ota);
+    sl[kSRJ] = j;
+    sl[kSRK] = k;
+    unsigned ub = nu;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, ub, o);
+      if (lane >= o) ub += y;
+    }
+    const unsigned NU = __shfl_sync(0xffffffffu, ub, 31);
+    sl[kSRUB] = ub - nu;
+    __syncwarp();
+
+    for (unsigned u0 = 0; u0 < NU; u0 += 32) {
+      // ---- units: lane = one active word ----
+      const unsigned e = u0 + lane;
+      const bool ve = e < NU;
+      int slot = 31, w = 0;
+      uint32_t m[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint32_t act = 0, qa = 0, qa1 = 0, qb = 0, qb1 = 0, qc = 0, qc1 = 0, qd = 0, qd1 = 0;
+      unsigned ntu = 0;
+      uint32_t sj = 0, sk = 0;
+      if (ve) {
+        slot = find_slot(SL, kSR, kSRUB, e);
+        const uint32_t* sr = SL + slot * kSR;
+        w = nth_set_bit_multi(UM + slot * kMaxAW, AW, (int)(e - sr[kSRUB]));
+        sj = sr[kSRJ];
+        sk = sr[kSRK];
+        const int64_t rr = (int64_t)sk * d.M + sj;
+        const int64_t rowbit = rr * L;
+        const bool hy = sj + 1 < M32, hz = (int64_t)sk + 1 < d.N, hc = hy && hz;
+        uint32_t an, bn = 0, cn = 0, dn = 0;
+        qa = row_word_next(W.bits, rowbit, w, L, &an);
+        if (hy) qb = row_word_next(W.bits, rowbit + L, w, L, &bn);
+        if (hz) qc = row_word_next(W.bits, rowbit + plane, w, L, &cn);
+        if (hc) qd = row_word_next(W.bits, rowbit + plane + L, w, L, &dn);
+        const uint32_t xm = low_mask((int)min(L - 1 - 32 * (int64_t)w, (int64_t)32));
+        qa1 = (qa >> 1) | (an << 31);
+        qb1 = (qb >> 1) | (bn << 31);
+        qc1 = (qc >> 1) | (cn << 31);
+        qd1 = (qd >> 1) | (dn << 31);
+        m[0] = (qa ^ qa1) & xm;
+        m[1] = hy ? (qa ^ qb) : 0u;
+        m[2] = hz ? (qa ^ qc) : 0u;
+        m[3] = (qb ^ qb1) & xm;
+        m[4] = (qc ^ qc1) & xm;
+        m[5] = (qd ^ qd1) & xm;
+        m[6] = hc ? (qc ^ qd) : 0u;
+        m[7] = hc ? (qb ^ qd) : 0u;
+        if (hc) {
+          const uint32_t u = (qa ^ qb) | (qa ^ qc) | (qa ^ qd);
+          const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
+          act = (u | (u >> 1) | (un << 31) | (qa ^ qa1)) & xm;
+          ntu = tri_count_word(qa, qa1, qb, qb1, qc, qc1, qd, qd1, xm);
+          if (A.mask && act) {
+            const int64_t cell0 = ((int64_t)sk * d.ny + sj) * d.nx + 32 * (int64_t)w;
+            uint32_t t = act;
+            while (t) {
+              const int bit = __ffs(t) - 1;
+              t &= t - 1;
+              if (__ldg(A.mask + cell0 + bit) != 0) {
+                ntu -= (unsigned)(s_case[cell_case(bit, qa, qa1, qb, qb1, qc, qc1, qd, qd1)] >> 60);
+                act &= ~(1u << bit);
+              }
+            }
+          }
+        }
+      }
+      // Per-row (segmented) prefixes of the eight crossing counts and the
+      // triangle count, carried across batches through the row slot.
+      const int key = ve ? slot : -1;
+      unsigned ex[5], tot[5];
+      bool last = false;
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        ex[t] = seg_excl(__popc(m[2 * t]) | (__popc(m[2 * t + 1]) << 16), key, &tot[t], &last);
+      ex[4] = seg_excl(ntu, key, &tot[4], &last);
+      uint32_t* rec = U + lane * kUR;
+      uint32_t* sr = SL + slot * kSR;
+      if (ve) {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          rec[kURMask + g] = m[g];
+          const unsigned ee = (g & 1) ? (ex[g >> 1] >> 16) : (ex[g >> 1] & 0xffffu);
+          st_i64(rec + kUROff + 2 * g, ld_i64(sr + kSROff + 2 * g) + ee);
+        }
+        st_i64(rec + kURTri, ld_i64(sr + kSRTri) + ex[4]);
+        rec[kURAct] = act;
+        rec[kURBits + 0] = qa; rec[kURBits + 1] = qa1;
+        rec[kURBits + 2] = qb; rec[kURBits + 3] = qb1;
+        rec[kURBits + 4] = qc; rec[kURBits + 5] = qc1;
+        rec[kURBits + 6] = qd; rec[kURBits + 7] = qd1;
+        rec[kURSlot] = (uint32_t)slot;
+        rec[kURW] = (uint32_t)w;
+      }
+      __syncwarp();
+      if (ve && last) {  // advance the row's running offsets past this batch
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          const unsigned tt = (g & 1) ? (tot[g >> 1] >> 16) : (tot[g >> 1] & 0xffffu);
+          st_i64(sr + kSROff + 2 * g, ld_i64(sr + kSROff + 2 * g) + tt);
+        }
+        st_i64(sr + kSRTri, ld_i64(sr + kSRTri) + tot[4]);
+      }
+      // Batch-wide work lists: points of the unit's own row, active cells.
+      const unsigned np = __popc(m[0]) + __popc(m[1]) + __popc(m[2]);
+      const unsigned nc = __popc(act);
+      unsigned wl = np | (nc << 16);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, wl, o);
+        if (lane >= o) wl += y;
+      }
+      const unsigned wtot = __shfl_sync(0xffffffffu, wl, 31);
+      const unsigned NP = wtot & 0xffffu, NC = wtot >> 16;
+      wl -= np | (nc << 16);
+      rec[kURPB] = ve ? (wl & 0xffffu) : 0xffffffffu;
+      rec[kURCB] = ve ? (wl >> 16) : 0xffffffffu;
+      __syncwarp();
+
+      // ---- points: lane = one crossing ----
+      for (unsigned p0 = 0; p0 < NP; p0 += 32) {
+        const unsigned pe = p0 + lane;
+        if (pe < NP) {
+          const int u = find_slot(U, kUR, kURPB, pe);
+          const uint32_t* R = U + u * kUR;
+          int kk = (int)(pe - R[kURPB]);
+          const uint32_t m0 = R[0], m1 = R[1], m2 = R[2];
+          const int c0 = __popc(m0), c1 = __popc(m1);
+          int type;
+          uint32_t mm;
+          if (kk < c0) {
+            type = 0; mm = m0;
+          } else if (kk < c0 + c1) {
+            type = 1; mm = m1; kk -= c0;
+          } else {
+            type = 2; mm = m2; kk -= c0 + c1;
+          }
+          const int bit = nth_set_bit(mm, kk);
+          const uint32_t* sr2 = SL + R[kURSlot] * kSR;
+          const uint32_t uj = sr2[kSRJ], uk = sr2[kSRK];
+          const int64_t n = 32 * (int64_t)R[kURW] + bit;
+          const int64_t node = ((int64_t)uk * d.M + uj) * L + n;
+          const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
+          const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
+          const long long shift = type == 0 ? shiftX : (type == 1 ? shiftY : shiftZ);
+          const long long row = ld_i64(R + kUROff + 2 * type) + __popc(mm & ((1u << bit) - 1u)) +
+                                shift;
+          if (row < 0 || row >= A.points_cap) {
+            record_overflow(W.info);
+          } else {
+            const float t = interp_t(iso, s0, s1);
+            const float px = coord(x0, n, hx);
+            const float py = coord(y0, uj, hy);
+            const float pz = coord(z0, (int64_t)uk + A.k_offset, hz);
+            const float px1 = type == 0 ? coord(x0, n + 1, hx) : px;
+            const float py1 = type == 1 ? coord(y0, (int64_t)uj + 1, hy) : py;
+            const float pz1 = type == 2 ? coord(z0, (int64_t)uk + 1 + A.k_offset, hz) : pz;
+            float* o = A.points + row * 3;
+            o[0] = lerp_ref(px, px1, t);
+            o[1] = lerp_ref(py, py1, t);
+            o[2] = lerp_ref(pz, pz1, t);
+          }
+        }
+      }
+
+      // ---- triangles: lane = one active cell ----
+      for (unsigned c0 = 0; c0 < NC; c0 += 32) {
+        const unsigned ce = c0 + lane;
+        const bool vc = ce < NC;
+        int u = -1, cb = 0;
+        unsigned nt = 0;
+        uint64_t pkc = 0;
+        if (vc) {
+          u = find_slot(U, kUR, kURCB, ce);
+          const uint32_t* R = U + u * kUR;
+          cb = nth_set_bit(R[kURAct], (int)(ce - R[kURCB]));
+          const int cs = cell_case(cb, R[kURBits + 0], R[kURBits + 1], R[kURBits + 2],
+                                   R[kURBits + 3], R[kURBits + 4], R[kURBits + 5],
+                                   R[kURBits + 6], R[kURBits + 7]);
+          pkc = s_case[cs];
+          nt = (unsigned)(pkc >> 60);
+        }
+        unsigned tt;
+        bool lst;
+        const unsigned ex_in_unit = seg_excl(nt, u, &tt, &lst);
+        // Cells of one unit may span batches: continue from the unit's
+        // running triangle offset, then advance it.
+        const uint32_t* R = U + (vc ? u : 0) * kUR;
+        const long long tb = vc ? ld_i64(R + kURTri) : 0;
+        if (nt) {
+          const long long tpos = outT + tb + ex_in_unit;
+          if (tpos < 0 || tpos + nt > A.conn_cap) {
+            record_overflow(W.info);
+          } else {
+            const uint32_t below = (1u << cb) - 1u;
+            const uint32_t below1 = cb == 31 ? 0xffffffffu : ((2u << cb) - 1u);
+            int32_t* o = A.conn + tpos * 3;
+            for (unsigned t = 0; t < 3 * nt; ++t) {
+              const unsigned ed = (unsigned)(pkc >> (4 * t)) & 0xfu;
+              const unsigned gp = (unsigned)(kEdgeGroup >> (4 * ed)) & 0xfu;
+              const unsigned g = gp & 7u;
+              const uint32_t lim = (gp & 8u) ? below1 : below;
+              o[t] = (int32_t)(ld_i64(R + kUROff + 2 * g) + __popc(R[kURMask + g] & lim));
+            }
+          }
+        }
+        __syncwarp();
+        if (vc && lst) st_i64(U + u * kUR + kURTri, tb + tt);
+        __syncwarp();
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
 // per-cell classification (26_marching_cubes.py:435-450)
 // ------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads)
@@ -1264,7 +1678,7 @@ struct FeLayout {
   FeDims d;
   size_t k2_smem;  // dynamic shared memory of the count/scan kernel
   int64_t V, nwords, bits_stride;
-  size_t off_bits, off_cnt, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
+  size_t off_bits, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
   size_t reset_bytes;  // info + flags, zeroed before each scan
 };
@@ -1284,23 +1698,24 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   const int64_t W = (d.L + 31) / 32;
   if (W > (1 << 24)) return false;
   d.W = (int)W;
+  d.AW = (int)((W + 31) / 32);
   int S = 1, logS = 0;
   while (S < d.W && S < 32) { S <<= 1; ++logS; }
   d.S = S;
   d.logS = logS;
-  // K2: one thread per row up to 32 words per row; longer rows get 2^logP
-  // threads each (<= 32 words per thread while P <= 32).
-  int logP = 0;
-  while ((32 << logP) < d.W && logP < 5) ++logP;
-  const int64_t TR = kThreads >> logP;
+  // K2a tile: about 8192 staged words per run, a multiple of 8 segments.
+  const int G = 32 >> logS;
+  int64_t TR = 8192 / d.W;
+  if (TR > 256) TR = 256;
+  TR = (TR / (8 * G)) * (8 * G);
+  if (TR < 8 * G) TR = 8 * G;
   d.TR = (int)TR;
-  d.logP = logP;
+  d.logP = 0;
   d.ctiles = (d.R + TR - 1) / TR;
   d.ntiles = (d.R + kScanRows - 1) / kScanRows;
   d.S3 = S < 8 ? S : 8;
   d.logS3 = logS < 3 ? logS : 3;
-  const int64_t stage = (((TR + 1) * d.W + 3 + 8) + 3) & ~(int64_t)3;
-  f.k2_smem = (size_t)(2 * stage + 4 * TR) * 4;
+  f.k2_smem = (size_t)(2 * k2_stage_words((int)TR, d.W)) * 4;
   if (f.k2_smem > 200 * 1024) return false;  // rows longer than ~90k nodes
   if (d.R > 0xffffffffLL) return false;  // worklist holds uint32 row ids
   f.V = d.L * d.M * d.N;
@@ -1315,6 +1730,7 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.off_tot = o;    o = align_up(o + (size_t)niso * 4 * 8, 256);
   f.off_base = o;   o = align_up(o + (size_t)niso * 8 * 8, 256);
   f.off_cnt = o;    o = align_up(o + (size_t)niso * d.R * 4 * 4, 256);
+  f.off_wact = o;   o = align_up(o + (size_t)niso * d.R * d.AW * 4, 256);
   f.off_rowoff = o; o = align_up(o + (size_t)niso * d.R * 4 * 8, 256);
   f.off_work = o;   o = align_up(o + (size_t)niso * d.R * 4, 256);
   f.off_bits = o;   o = align_up(o + (size_t)niso * f.bits_stride * 4, 256);
@@ -1331,6 +1747,7 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
     w.bits = reinterpret_cast<uint32_t*>(b + f.off_bits) + (size_t)q * f.bits_stride;
     w.rowoff = reinterpret_cast<long long*>(b + f.off_rowoff) + (size_t)q * f.d.R * 4;
     w.cnt = reinterpret_cast<int*>(b + f.off_cnt) + (size_t)q * f.d.R * 4;
+    w.wact = reinterpret_cast<uint32_t*>(b + f.off_wact) + (size_t)q * f.d.R * f.d.AW;
     w.tot = reinterpret_cast<long long*>(b + f.off_tot) + (size_t)q * 4;
     w.work = reinterpret_cast<uint32_t*>(b + f.off_work) + (size_t)q * f.d.R;
     w.flags = reinterpret_cast<uint32_t*>(b + f.off_flags) + (size_t)q * f.d.ntiles;
@@ -1618,10 +2035,17 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
   }
   FeWsAll v = fe_views(f, ws, niso);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int G = 32 >> f.d.logS3;
-  const int g = grid_for(f.d.n_own_rows, (kThreads / 32) * G, 8);
-  dim3 grid((unsigned)g, (unsigned)niso);
-  k_fe_emit<<<grid, kThreads, 0, st>>>(f.d, v, A);
+  if (f.d.AW <= kMaxAW) {
+    const size_t smem = sizeof(EmitSmem);
+    TK_CUDA(cudaFuncSetAttribute(k_fe_emit_words, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+    const int g = grid_for(f.d.n_own_rows, kThreads, 3);
+    k_fe_emit_words<<<dim3((unsigned)g, (unsigned)niso), kThreads, smem, st>>>(f.d, v, A);
+  } else {
+    const int G = 32 >> f.d.logS3;
+    const int g = grid_for(f.d.n_own_rows, (kThreads / 32) * G, 8);
+    k_fe_emit_rows<<<dim3((unsigned)g, (unsigned)niso), kThreads, 0, st>>>(f.d, v, A);
+  }
   TK_LAUNCHED();
   return TKMC_OK;
 }

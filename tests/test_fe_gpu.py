@@ -195,3 +195,31 @@ def test_degenerate_grids_match_oracle(tack, oracle):
             assert got is None
         else:
             assert_same_surface(got, ref)
+
+
+@pytest.mark.parametrize("shape", [(1099, 3, 4), (2047, 4, 3), (1500, 5, 2), (4999, 2, 2),
+                                   (9000, 2, 1), (1023, 2, 2), (1024, 3, 2)])
+def test_long_rows_match_oracle(tack, oracle, shape):
+    """Rows longer than 1024 nodes: several threads per row in the count
+    pass, multi-word activity masks, and (beyond 8192 nodes) the row-wise
+    emit kernel."""
+    nx, ny, nz = shape
+    rng = np.random.default_rng(nx)
+    n = (nx + 1) * (ny + 1) * (nz + 1)
+    # Smooth along x with sparse crossings plus a few dense stretches.
+    i = np.arange(n) % (nx + 1)
+    v = (np.sin(i * 0.013 + rng.random()) + 0.3 * rng.standard_normal(n)).astype(np.float32)
+    g = (nx, ny, nz, 0.25, -1.0, 3.0, 0.5, 1.5, 0.75)
+    for iso in (0.0, 0.9):
+        got = capi_fe(v, g, [iso], want_rows=True)
+        ref = oracle.flying_edges(v, oracle.Grid(*g), iso)
+        info = oracle.count_block(v, oracle.Grid(*g), iso)
+        xo, yo, zo, to = reference_offsets_from_rows(got["rows"][0], got["counts"][0], g)
+        np.testing.assert_array_equal(xo, info["xo"])
+        np.testing.assert_array_equal(yo, info["yo"])
+        np.testing.assert_array_equal(zo, info["zo"])
+        np.testing.assert_array_equal(to, info["tri_offsets"])
+        if ref is None:
+            assert got["total_points"] == 0 or got["total_tris"] == 0
+        else:
+            assert_same_surface(got, ref)
