@@ -364,10 +364,12 @@ struct FeDims {
   int64_t nx, ny;       // cells per row, cell rows per plane (mask index)
   int64_t ntiles;       // K2b scan tiles
   int64_t ctiles;       // K2a count tiles
+  int64_t ctiles_a;     // K2a count tiles, word-aligned rows
   int W;                // 32-bit words per row
   int AW;               // words of the per-row activity mask = ceil(W / 32)
   int S, logS;          // lanes per row (power of two <= 32)
   int TR;               // K2 tile height in rows
+  int TRa;              // K2 tile height for word-aligned rows (0: not used)
   int logP;             // K2 threads per row = 1 << logP (TR << logP == block size)
   int S3, logS3;        // K3 lanes per row (<= 8: several rows per warp)
 };
@@ -672,6 +674,107 @@ k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nword
     count_rows<true>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
   else
     count_rows<false>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
+}
+
+// K2a for rows that start on a word (L % 32 == 0): one thread per row.
+//
+// The tile's bit rows [R0, R0+TR] and [R0+M, R0+M+TR] are copied with
+// 4-byte cp.async into shared memory rows of SW = W+1 words (odd stride,
+// a zero word after each row).  Thread t counts row R0+t word by word; the
+// 32 lanes of a warp are 32 consecutive rows at the same word index, so they
+// read distinct banks, and since the surface is spatially coherent most
+// words are free of side changes in all 32 rows at once and cost a warp
+// only the loads and one vote.
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(gmem) : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_fe_count_aligned(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
+  extern __shared__ uint32_t k2_smem[];
+  __shared__ int s_ntri[256];
+  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
+  const int TR = d.TRa, W = d.W, SW = d.W + 1, AW = d.AW;
+  uint32_t* sA = k2_smem;                // (TR+1) rows of SW words
+  uint32_t* sC = k2_smem + (TR + 1) * SW;
+  for (int i = tid; i < 256; i += blockDim.x) s_ntri[i] = (int)(c_case_tris[i] >> 60);
+  const int64_t R0 = (int64_t)blockIdx.x * TR;
+  for (int rl = warp; rl <= TR; rl += nwarp) {
+    const int64_t ra = R0 + rl, rc = R0 + d.M + rl;
+    uint32_t* da = sA + rl * SW;
+    uint32_t* dc = sC + rl * SW;
+    for (int w = lane; w < W; w += 32) {
+      if (ra < d.R) cp_async4(da + w, Wk.bits + ra * W + w);
+      if (rc < d.R) cp_async4(dc + w, Wk.bits + rc * W + w);
+    }
+    if (lane == 0) {
+      da[W] = 0u;
+      dc[W] = 0u;
+    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  const int64_t r = R0 + tid;
+  const bool valid = tid < TR && r < d.R;
+  const uint32_t M32 = (uint32_t)d.M;
+  const uint32_t j = valid ? (uint32_t)r % M32 : 0u, k = valid ? (uint32_t)r / M32 : 0u;
+  const bool hasY = valid && (j + 1 < M32);
+  const bool hasZ = valid && ((int64_t)k + 1 < d.N);
+  const bool hasC = hasY && hasZ;
+  const uint32_t* pa = sA + (valid ? tid : 0) * SW;
+  const uint32_t* pb = pa + SW;
+  const uint32_t* pc = sC + (valid ? tid : 0) * SW;
+  const uint32_t* pd = pc + SW;
+  const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
+  const int Li = (int)d.L;
+  unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
+  uint32_t amask = 0;
+  for (int w = 0; w < W; ++w) {
+    const uint32_t a = valid ? pa[w] : 0u, an = valid ? (pa[w + 1] & 1u) : 0u;
+    uint32_t b = a, bn = an, c = a, cn = an, dd, dn;
+    if (hasY) { b = pb[w]; bn = pb[w + 1] & 1u; }
+    if (hasZ) { c = pc[w]; cn = pc[w + 1] & 1u; }
+    dd = b; dn = bn;
+    if (hasC) { dd = pd[w]; dn = pd[w + 1] & 1u; }
+    const uint32_t a1 = (a >> 1) | (an << 31);
+    const uint32_t uu = (a ^ b) | (a ^ c) | (a ^ dd);
+    const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
+    const bool busy = (uu | (a ^ a1) | (un << 31)) != 0u;
+    if (__any_sync(0xffffffffu, busy) && busy) {
+      const uint32_t xm = low_mask(Li - 1 - 32 * w);
+      const unsigned x0 = __popc((a ^ a1) & xm);
+      const unsigned y0 = __popc(a ^ b);
+      const unsigned z0 = __popc(a ^ c);
+      unsigned t0 = 0;
+      if (hasC) {
+        const uint32_t b1 = (b >> 1) | (bn << 31), c1 = (c >> 1) | (cn << 31);
+        const uint32_t d1 = (dd >> 1) | (dn << 31);
+        t0 = tri_count_word(a, a1, b, b1, c, c1, dd, d1, xm);
+        if (mask) {  // masked cells emit nothing: take their triangles back out
+          uint32_t act = (uu | (uu >> 1) | (un << 31) | (a ^ a1)) & xm;
+          while (act) {
+            const int bit = __ffs(act) - 1;
+            act &= act - 1;
+            if (__ldg(mask + cell_row0 + 32 * w + bit) != 0)
+              t0 -= (unsigned)s_ntri[cell_case(bit, a, a1, b, b1, c, c1, dd, d1)];
+          }
+        }
+      }
+      cX += x0;
+      cY += y0;
+      cZ += z0;
+      cT += t0;
+      if (x0 | y0 | z0 | t0) amask |= 1u << (w & 31);
+    }
+    if ((w & 31) == 31 || w == W - 1) {
+      if (valid) Wk.wact[r * AW + (w >> 5)] = amask;
+      amask = 0;
+    }
+  }
+  if (valid) reinterpret_cast<int4*>(Wk.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
 }
 
 // K2b: single-pass (decoupled look-back) exclusive scan of the row counts
@@ -1676,7 +1779,8 @@ k_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive, uint32_t* 
 
 struct FeLayout {
   FeDims d;
-  size_t k2_smem;  // dynamic shared memory of the count/scan kernel
+  size_t k2_smem;   // dynamic shared memory of the count kernel
+  size_t k2a_smem;  // ... of the word-aligned count kernel
   int64_t V, nwords, bits_stride;
   size_t off_bits, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
@@ -1716,7 +1820,20 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   d.S3 = S < 8 ? S : 8;
   d.logS3 = logS < 3 ? logS : 3;
   f.k2_smem = (size_t)(2 * k2_stage_words((int)TR, d.W)) * 4;
-  if (f.k2_smem > 200 * 1024) return false;  // rows longer than ~90k nodes
+  // Word-aligned rows: one thread per row, two staged runs of TRa+1 rows of
+  // W+1 words within ~200 KiB of shared memory.
+  d.TRa = 0;
+  if ((d.L & 31) == 0) {
+    int64_t t = 25600 / (d.W + 1) - 1;
+    if (t > 256) t = 256;
+    t = (t / 32) * 32;
+    if (t >= 32) {
+      d.TRa = (int)t;
+      d.ctiles_a = (d.R + t - 1) / t;
+      f.k2a_smem = (size_t)(2 * (t + 1) * (d.W + 1)) * 4;
+    }
+  }
+  if (d.TRa == 0 && f.k2_smem > 200 * 1024) return false;  // rows longer than ~90k nodes
   if (d.R > 0xffffffffLL) return false;  // worklist holds uint32 row ids
   f.V = d.L * d.M * d.N;
   f.nwords = (f.V + 31) / 32;
@@ -1901,10 +2018,11 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   for (int t = 0; t < niso; ++t) iso.v[t] = isovalues[t];
   FeWsAll v = fe_views(f, ws, niso);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int vec = (reinterpret_cast<uintptr_t>(scalar) % 16) == 0;
   const int64_t nchunks = (f.V + 1023) / 1024;
   const int g = grid_for(nchunks, kThreads / 32, 8);
   uint32_t* bits0 = v.iso[0].bits;
-  if ((reinterpret_cast<uintptr_t>(scalar) % 16) == 0)
+  if (vec)
     k_fe_threshold_v4<<<g, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0, f.bits_stride,
                                               f.nwords);
   else
@@ -1925,11 +2043,19 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   TK_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + f.off_info, 0, f.reset_bytes - f.off_info, st));
   const int64_t skip = g_skip_tile.exchange(-1);
-  if (f.k2_smem > 48 * 1024)
-    TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)f.k2_smem));
-  k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso), kThreads, f.k2_smem, st>>>(
-      f.d, v, mask, f.nwords);
+  if (f.d.TRa > 0) {
+    if (f.k2a_smem > 48 * 1024)
+      TK_CUDA(cudaFuncSetAttribute(k_fe_count_aligned,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)f.k2a_smem));
+    k_fe_count_aligned<<<dim3((unsigned)f.d.ctiles_a, (unsigned)niso), f.d.TRa, f.k2a_smem,
+                         st>>>(f.d, v, mask);
+  } else {
+    if (f.k2_smem > 48 * 1024)
+      TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)f.k2_smem));
+    k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso), kThreads, f.k2_smem, st>>>(
+        f.d, v, mask, f.nwords);
+  }
   TK_LAUNCHED();
   k_fe_scan_rows<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
       f.d, v, g_wait_ns.load(), skip);
