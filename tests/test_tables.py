@@ -60,3 +60,24 @@ def test_edges_join_adjacent_corners():
     for e in range(12):
         a, b = corner[edges[2 * e]], corner[edges[2 * e + 1]]
         assert sum(x != y for x, y in zip(a, b)) == 1
+
+
+def test_closed_form_triangle_count():
+    """The count pass computes a cell's triangle count without the table:
+    ntri = V - 2F - 4*belt + 4*full, V = corners above, F = faces whose four
+    corners are above, belt = exactly two antipodal corners below, full = all
+    eight above.  It must equal the table's count for every case."""
+    _, num, _ = _lib_tables()
+    corner = [(0, 0, 0), (1, 0, 0), (1, 1, 0), (0, 1, 0), (0, 0, 1), (1, 0, 1), (1, 1, 1), (0, 1, 1)]
+    faces = [[c for c in range(8) if corner[c][ax] == side] for ax in range(3) for side in (0, 1)]
+    antipodal = [(a, b) for a in range(8) for b in range(a + 1, 8)
+                 if all(corner[a][d] != corner[b][d] for d in range(3))]
+    assert len(antipodal) == 4
+    for case in range(256):
+        above = [(case >> c) & 1 for c in range(8)]
+        v = sum(above)
+        f = sum(all(above[c] for c in face) for face in faces)
+        below = {c for c in range(8) if not above[c]}
+        belt = int(len(below) == 2 and tuple(sorted(below)) in antipodal)
+        full = int(v == 8)
+        assert v - 2 * f - 4 * belt + 4 * full == num[case], case
