@@ -89,6 +89,24 @@ int tkmc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive,
                   void* workspace, size_t workspace_bytes, int64_t* total,
                   void* stream);
 
+/* tkmc_scan_i32 without any device allocation, for callers that cannot
+ * allocate: code called from inside another application's time step (an
+ * in-situ hook in a simulation that has reserved the GPU's memory up front,
+ * where cudaMalloc can fail or stall the application's other streams by
+ * synchronising the device), or hosts whose allocator is owned by another
+ * framework.  Same arguments and results as tkmc_scan_i32, minus the
+ * workspace.  No counterpart in the reference (its scan allocates fields,
+ * scan.py:94-101).
+ * Scratch is a static device array inside this library (about 320 KiB,
+ * held by every GPU that loads it until the process exits); n is limited to
+ * 2^26 = 67,108,864 values and larger n returns TKMC_ERR_INVALID_ARG.  The
+ * first call on a device looks up the array's device address (a synchronous
+ * runtime call): make that first call before any stream capture.  All calls
+ * share the one array: calls that overlap on the GPU (other streams or
+ * threads, same device) race, so serialise them. */
+int tkmc_scan_i32_noalloc(const int32_t* in, int32_t* out, int64_t n,
+                          int inclusive, int64_t* total, void* stream);
+
 /* ---- flying edges (merged-point marching cubes) ------------------------- */
 /*
  * Grid: nx, ny, nz cells; (nx+1)*(ny+1)*(nz+1) f32 node values, i fastest,

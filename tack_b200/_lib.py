@@ -36,6 +36,7 @@ SIGNATURES = {
     "tkmc_reduce_f32": (_I, [_P, _I64, _P, _SZ, _P, _P]),
     "tkmc_scan_workspace_bytes": (_SZ, [_I64]),
     "tkmc_scan_i32": (_I, [_P, _P, _I64, _I, _P, _SZ, _P, _P]),
+    "tkmc_scan_i32_noalloc": (_I, [_P, _P, _I64, _I, _P, _P]),
     "tkmc_fe_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I]),
     "tkmc_fe_count": (_I, [_P, _I64, _I64, _I64, _I, _P, _I, _P, _P, _SZ, _P, _P]),
     "tkmc_fe_emit": (_I, [_P, _I64, _I64, _I64, _I, _I64, _P, _P, _I, _P, _P, _SZ,

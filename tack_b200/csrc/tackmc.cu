@@ -1900,6 +1900,47 @@ int grid_for(int64_t work_items, int per_block, int blocks_per_sm) {
   return (int)g;
 }
 
+// ------------------------------------------------------------------------
+// scan without allocation: scratch in a static device array
+// ------------------------------------------------------------------------
+//
+// For callers that cannot allocate device memory, tkmc_scan_i32_noalloc
+// keeps the scan's tile states in this file-scope array instead of a
+// caller-provided workspace.  Every GPU that loads the library holds it
+// (about 320 KiB) until the process exits.  The layout is the one
+// tkmc_scan_i32 uses for its workspace, sized for the largest accepted n.
+constexpr int64_t kNoAllocScanMaxN = (int64_t)1 << 26;  // 67,108,864 values
+constexpr int64_t kNoAllocScanTiles = kNoAllocScanMaxN / kScanTile;
+constexpr size_t kNoAllocFlagsBytes = ((size_t)kNoAllocScanTiles * 4 + 255) / 256 * 256;
+constexpr size_t kNoAllocTileBytes = ((size_t)kNoAllocScanTiles * 8 + 255) / 256 * 256;
+constexpr size_t kNoAllocScratchBytes = 256 + kNoAllocFlagsBytes + 2 * kNoAllocTileBytes;
+
+__device__ __align__(256) unsigned char g_noalloc_scan_scratch[kNoAllocScratchBytes];
+
+// Device address of g_noalloc_scan_scratch on the current device, resolved
+// once per device.  In host code the array's name is only a host-side
+// stand-in; kernels must be given this address.
+int noalloc_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* cache[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return set_err(TKMC_ERR_CUDA, "cudaGetDevice failed: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_err(TKMC_ERR_INVALID_ARG, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scan_scratch);
+    if (e != cudaSuccess || !p)
+      return set_err(TKMC_ERR_CUDA, "cudaGetSymbolAddress(scan scratch) failed: %s",
+                     cudaGetErrorString(e));
+    cache[dev] = p;
+  }
+  *out = cache[dev];
+  return TKMC_OK;
+}
+
 }  // namespace
 
 // ==========================================================================
@@ -1985,6 +2026,45 @@ int tkmc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive, voi
   const int64_t skip = g_skip_tile.exchange(-1);
   k_scan_i32<<<(unsigned)tiles, kThreads, 0, st>>>(in, out, n, inclusive, flags, agg, incl, info,
                                                    g_wait_ns.load(), skip);
+  TK_LAUNCHED();
+  if (total) {
+    long long h[3];
+    TK_CUDA(cudaMemcpyAsync(h, info, sizeof(h), cudaMemcpyDeviceToHost, st));
+    TK_CUDA(cudaStreamSynchronize(st));
+    if (h[2]) return set_err(TKMC_ERR_DEVICE_TIMEOUT, "scan look-back wait expired");
+    *total = h[1];
+  }
+  return TKMC_OK;
+}
+
+int tkmc_scan_i32_noalloc(const int32_t* in, int32_t* out, int64_t n, int inclusive,
+                          int64_t* total, void* stream) {
+  if (n < 0 || (n > 0 && (!in || !out)))
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_scan_i32_noalloc: bad arguments");
+  if (n > kNoAllocScanMaxN)
+    return set_err(TKMC_ERR_INVALID_ARG,
+                   "tkmc_scan_i32_noalloc: n = %lld exceeds the static scratch limit of %lld "
+                   "values; use tkmc_scan_i32 with a workspace",
+                   (long long)n, (long long)kNoAllocScanMaxN);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n == 0) {
+    if (total) *total = 0;
+    return TKMC_OK;
+  }
+  void* scratch = nullptr;
+  int rc = noalloc_scratch_address(&scratch);
+  if (rc) return rc;
+  const int64_t tiles = (n + kScanTile - 1) / kScanTile;
+  char* b = static_cast<char*>(scratch);
+  long long* info = reinterpret_cast<long long*>(b);  // 0 counter, 1 total, 2 error
+  uint32_t* flags = reinterpret_cast<uint32_t*>(b + 256);
+  long long* agg = reinterpret_cast<long long*>(b + 256 + kNoAllocFlagsBytes);
+  long long* incl = reinterpret_cast<long long*>(b + 256 + kNoAllocFlagsBytes + kNoAllocTileBytes);
+  // The array keeps the previous call's contents: the tile counter, the
+  // error word and the tile flags must start at zero.
+  TK_CUDA(cudaMemsetAsync(scratch, 0, 256 + align_up((size_t)tiles * 4, 256), st));
+  k_scan_i32<<<(unsigned)tiles, kThreads, 0, st>>>(in, out, n, inclusive, flags, agg, incl, info,
+                                                   g_wait_ns.load(), -1);
   TK_LAUNCHED();
   if (total) {
     long long h[3];
