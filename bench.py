@@ -374,7 +374,9 @@ def main():
                 "volume_nodes": list(shape), "cells": cells, "isovalues": isos,
                 "parallelism": (f"z-slab x{world} (ghost plane, one NCCL all-gather of totals)"
                                 if world > 1 else "single GPU"),
-                "l2": "inputs larger than L2 (f32 volume 4 GiB >> 126 MB L2), no flush",
+                "l2": (f"inputs larger than L2 (f32 slab {4.0 * local_nodes / 2**30:.2f} GiB per "
+                       f"GPU vs 126 MB L2), no flush" if 4.0 * local_nodes > 126e6 * 2 else
+                       "input smaller than 2x L2: numbers include L2 reuse between steps"),
             },
             "roofline": {
                 "bound": "hbm", "kernel": "k_fe_threshold (K1: volume -> node bitmask)",
@@ -419,16 +421,32 @@ def run_e2e(args, tack, torch, dist, vol, grid, plan, eng, isos, world, rank, de
 
     def once():
         nonlocal d2h
-        dvol.copy_(host, non_blocking=True)
         if world == 1:
-            r = tack.flying_edges(tack.from_torch(dvol), grid, isos if len(isos) > 1 else isos[0])
+            # The public call on a pinned host tensor: H2D, filter, D2H.
+            r = tack.flying_edges(host, grid, isos if len(isos) > 1 else isos[0])
             d2h = r["points"].nbytes + r["conn"].nbytes
         else:
+            dvol.copy_(host, non_blocking=True)
             r = eng.run(dvol)
-            p = r["points_field"].tensor.cpu()
-            c = r["conn_field"].tensor.cpu()
+            p = torch.empty(r["points_field"].tensor.shape, dtype=torch.float32, pin_memory=True)
+            c = torch.empty(r["conn_field"].tensor.shape, dtype=torch.int32, pin_memory=True)
+            p.copy_(r["points_field"].tensor, non_blocking=True)
+            c.copy_(r["conn_field"].tensor, non_blocking=True)
+            stream.synchronize()
             d2h = p.numel() * 4 + c.numel() * 4
         return r
+
+    def h2d_link_ms(reps=3):
+        """Bare pinned host->device copy of the same bytes (the link bound)."""
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            dvol.copy_(host, non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
 
     once()
     torch.cuda.synchronize()
@@ -447,12 +465,15 @@ def run_e2e(args, tack, torch, dist, vol, grid, plan, eng, isos, world, rank, de
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         dist.all_reduce(tot)
     ms = float(ms.item())
+    link = h2d_link_ms()
     return {"value": cells * args.e2e_steps / (ms * 1e-3) / 1e9, "unit": "Gcells/s",
             "h2d_bytes_per_step": int(tot[0].item()), "d2h_bytes_per_step": int(tot[1].item()),
             "ms_per_step": ms / args.e2e_steps, "steps": args.e2e_steps,
-            "path": ("tack_b200.flying_edges (pinned host -> device volume copy, "
-                     "points/conn copied back to numpy)" if world == 1 else
-                     "tack_b200.distributed SlabEngine.run per rank + D2H of its slices")}
+            "h2d_copy_alone_ms": link, "h2d_copy_alone_gbs": h2d / (link * 1e-3) / 1e9,
+            "path": ("tack_b200.flying_edges(pinned host tensor): H2D of the volume, "
+                     "count, emit, points/conn copied back into pinned numpy arrays"
+                     if world == 1 else
+                     "per rank: pinned H2D of its slab, SlabEngine.run, D2H of its slices")}
 
 
 if __name__ == "__main__":

@@ -169,7 +169,9 @@ def flying_edges(scalar, grid, isovalue, *, copy_to_host=True):
     Args:
         scalar: f32 field of node values, (nx+1)*(ny+1)*(nz+1) values with i
             fastest (a tack_b200 Field, a torch CUDA tensor, a reference tack
-            field on its CUDA backend, or a numpy array).
+            field on its CUDA backend, or a host array: a numpy array or CPU
+            tensor is copied to the device first, asynchronously when the
+            tensor is pinned).
         grid: UniformGrid.
         isovalue: threshold, or a sequence of thresholds.
 
@@ -274,9 +276,18 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
 
     points_field = Field(f32, (total_points * 3,), CUDABuffer(points_t))
     conn_field = Field(i32, (total_tris * 3,), CUDABuffer(conn_t))
+    points_h = conn_h = None
+    if copy_to_host:
+        # Page-locked destinations: the copies run at full link speed and
+        # the returned numpy arrays keep their pinned blocks alive.
+        points_h = torch.empty(points_t.shape, dtype=points_t.dtype, pin_memory=True)
+        conn_h = torch.empty(conn_t.shape, dtype=conn_t.dtype, pin_memory=True)
+        points_h.copy_(points_t, non_blocking=True)
+        conn_h.copy_(conn_t, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
     out = {
-        "points": points_t.cpu().numpy().reshape(-1, 3) if copy_to_host else None,
-        "conn": conn_t.cpu().numpy().reshape(-1, 3) if copy_to_host else None,
+        "points": points_h.numpy().reshape(-1, 3) if copy_to_host else None,
+        "conn": conn_h.numpy().reshape(-1, 3) if copy_to_host else None,
         "points_field": points_field,
         "conn_field": conn_field,
         "total_points": total_points,

@@ -86,6 +86,25 @@ def slab_bases(all_counts, rank):
             "totals": np.stack([P, tot[:, 3]], axis=1)}
 
 
+def gather_counts(counts, world, group=None, device=None, out=None):
+    """All-gather every rank's totals: ONE collective of 4 int64 per
+    isovalue per rank.  counts: int64 [niso, 4] on the host.  device is the
+    process group's device (a CUDA device for NCCL, cpu for gloo); out an
+    optional preallocated [world*niso*4] int64 tensor there.  Returns int64
+    [world, niso, 4] on the host."""
+    import torch.distributed as dist
+    c = np.ascontiguousarray(np.asarray(counts, np.int64).reshape(-1))
+    niso = c.size // 4
+    if world == 1:
+        return c.reshape(1, niso, 4)
+    device = torch.device("cpu") if device is None else device
+    src = torch.from_numpy(c).to(device)
+    if out is None:
+        out = torch.empty(world * c.size, dtype=torch.int64, device=device)
+    dist.all_gather_into_tensor(out, src, group=group)
+    return out.cpu().numpy().reshape(world, niso, 4)
+
+
 def _i64(vals):
     flat = [int(v) for v in np.asarray(vals).reshape(-1)]
     return (ctypes.c_int64 * len(flat))(*flat)
@@ -108,7 +127,6 @@ class SlabEngine:
         nx, ny = grid.nx, grid.ny
         self.nbytes = self.lib.tkmc_fe_workspace_bytes(nx, ny, plan.nz_cells, len(self.isos))
         self.ws = torch.empty(self.nbytes, dtype=torch.uint8, device=self.dev)
-        self.counts_dev = torch.zeros(len(self.isos) * 4, dtype=torch.int64, device=self.dev)
         world = plan.world
         self.gathered = torch.zeros(world * len(self.isos) * 4, dtype=torch.int64,
                                     device=self.dev)
@@ -125,13 +143,7 @@ class SlabEngine:
 
     def exchange(self, counts):
         """All-gather every rank's totals (one collective)."""
-        import torch.distributed as dist
-        niso = len(self.isos)
-        if self.plan.world == 1:
-            return counts.reshape(1, niso, 4)
-        self.counts_dev.copy_(torch.from_numpy(counts.reshape(-1)))
-        dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
-        return self.gathered.cpu().numpy().reshape(self.plan.world, niso, 4)
+        return gather_counts(counts, self.plan.world, self.group, self.dev, self.gathered)
 
     def emit(self, local_values, counts, bases):
         g, p, lib = self.grid, self.plan, self.lib

@@ -175,13 +175,14 @@ def device_tensor(obj, dtype=f32):
     """Resolve a field-like object to a flat contiguous CUDA tensor.
 
     Accepts a tack_b200 Field, a torch CUDA tensor, a reference tack field on
-    its CUDA backend (anything with ``_buffer.device_ptr`` and ``shape``), or
-    a numpy array (copied to the device).
+    its CUDA backend (anything with ``_buffer.device_ptr`` and ``shape``), a
+    CPU tensor (copied on the current stream; without a host wait when it is
+    pinned) or a numpy array (copied to the device).
     """
     if isinstance(obj, Field):
         t = obj.tensor
     elif isinstance(obj, torch.Tensor):
-        t = obj if obj.is_cuda else obj.to(current_device())
+        t = obj if obj.is_cuda else obj.to(current_device(), non_blocking=obj.is_pinned())
         t = t.reshape(-1)
         if not t.is_contiguous():
             t = t.contiguous()

@@ -1,0 +1,61 @@
+"""One rank of the z-slab flying-edges path under torchrun (NCCL).
+
+Each rank generates only its own planes (plus the ghost plane) of a 256^3
+blobs volume, runs SlabEngine (count -> one all-gather of totals -> emit)
+and sends its slices to rank 0, which assembles them and compares the result
+with a single-volume flying_edges call on its own GPU.  Rank 0 writes "ok"
+to the file named by argv[1] when they are identical.
+"""
+
+import os
+import sys
+from datetime import timedelta
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+import tack_b200 as tack  # noqa: E402
+from tack_b200 import workloads  # noqa: E402
+from tack_b200.distributed import SlabEngine, SlabPlan, assemble  # noqa: E402
+
+
+def main():
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    ok = False
+    try:
+        tack.init(tack.cuda)
+        shape = (256, 256, 256)
+        nx, ny, nz = shape[0] - 1, shape[1] - 1, shape[2] - 1
+        grid = tack.UniformGrid(nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+        plan = SlabPlan(shape[2], world, rank)
+        vals = workloads.generate("blobs", shape, plan.k0, plan.k1)
+        r = SlabEngine(grid, plan, [0.5]).run(vals)
+        part = {"points": r["points_field"].tensor.cpu().numpy(),
+                "conn": r["conn_field"].tensor.cpu().numpy(),
+                "counts": r["counts"], "bases": r["bases"]}
+        parts = [None] * world
+        dist.all_gather_object(parts, part)
+        if rank == 0:
+            points, conn = assemble(parts)
+            whole = workloads.generate("blobs", shape)
+            ref = tack.flying_edges(tack.from_torch(whole), grid, 0.5)
+            ok = (np.array_equal(conn, ref["conn"]) and
+                  np.array_equal(points.view(np.uint32), ref["points"].view(np.uint32)))
+            with open(sys.argv[1], "w") as f:
+                f.write("ok\n" if ok else "mismatch\n")
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+    return 0 if (ok or rank != 0) else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
