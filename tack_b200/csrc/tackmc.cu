@@ -270,9 +270,23 @@ __device__ void lookback(uint32_t* flags, long long* agg, long long* incl,
 // 512-byte float4 loads, issued before any use.  Four ballots per load give
 // the "above" bits in lane-interleaved order; each lane assembles one 32-bit
 // word of node order and the warp stores 32 words (128 B) coalesced.
+//
+// The same step leaves a summary of its 32 words: sums[ch] = {mixed, ones},
+// bit w of `mixed` set when word 32*ch + w has nodes on both sides, bit w of
+// `ones` when all its nodes are above.  The count pass reads these 8 bytes
+// per 1024 nodes to find the few words where anything can change.
+
+// Summary of the 32 words held by the warp's lanes (one word per lane).
+__device__ __forceinline__ void store_summary(uint2* sums, int64_t ch, uint32_t word, int lane) {
+  const uint32_t mixed = __ballot_sync(0xffffffffu, word != 0u && word != 0xffffffffu);
+  const uint32_t ones = __ballot_sync(0xffffffffu, word == 0xffffffffu);
+  if (lane == 0) sums[ch] = make_uint2(mixed, ones);
+}
+
 __global__ void __launch_bounds__(kThreads)
 k_fe_threshold_v4(const float* __restrict__ v, int64_t n, IsoParams iso, int niso,
-                  uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords) {
+                  uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
+                  uint2* __restrict__ sums, int64_t sums_stride) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -281,6 +295,8 @@ k_fe_threshold_v4(const float* __restrict__ v, int64_t n, IsoParams iso, int nis
   if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
     const int t = threadIdx.x >> 3;
     if (t < niso) bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;  // padding
+    if (t < niso && (threadIdx.x & 7) < 2)
+      sums[t * sums_stride + nchunks + (threadIdx.x & 7)] = make_uint2(0u, 0u);
   }
   for (int64_t ch = warp; ch < nchunks; ch += nwarps) {
     const int64_t base = ch << 10;
@@ -314,6 +330,7 @@ k_fe_threshold_v4(const float* __restrict__ v, int64_t n, IsoParams iso, int nis
                  (spread8(b2 >> sh) << 2) | (spread8(b3 >> sh) << 3);
       }
       if (wi < nwords) bits[t * bits_stride + wi] = word;
+      store_summary(sums + t * sums_stride, ch, word, lane);
     }
   }
 }
@@ -322,7 +339,8 @@ k_fe_threshold_v4(const float* __restrict__ v, int64_t n, IsoParams iso, int nis
 // coalesced loads per warp step, one ballot per word.
 __global__ void __launch_bounds__(kThreads)
 k_fe_threshold_scalar(const float* __restrict__ v, int64_t n, IsoParams iso, int niso,
-                      uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords) {
+                      uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
+                      uint2* __restrict__ sums, int64_t sums_stride) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -330,6 +348,8 @@ k_fe_threshold_scalar(const float* __restrict__ v, int64_t n, IsoParams iso, int
   if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
     const int t = threadIdx.x >> 3;
     if (t < niso) bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;
+    if (t < niso && (threadIdx.x & 7) < 2)
+      sums[t * sums_stride + nchunks + (threadIdx.x & 7)] = make_uint2(0u, 0u);
   }
   for (int64_t ch = warp; ch < nchunks; ch += nwarps) {
     const int64_t base = ch << 10;
@@ -349,6 +369,7 @@ k_fe_threshold_scalar(const float* __restrict__ v, int64_t n, IsoParams iso, int
         if (lane == q) word = b;
       }
       if (wi < nwords) bits[t * bits_stride + wi] = word;
+      store_summary(sums + t * sums_stride, ch, word, lane);
     }
   }
 }
@@ -363,13 +384,11 @@ struct FeDims {
   int64_t n_own_rows;   // rows this slab owns (R, or R - M with a ghost plane)
   int64_t nx, ny;       // cells per row, cell rows per plane (mask index)
   int64_t ntiles;       // K2b scan tiles
-  int64_t ctiles;       // K2a count tiles
-  int64_t ctiles_a;     // K2a count tiles, word-aligned rows
+  int64_t ctiles;       // K2a count tiles (rows not word-aligned)
   int W;                // 32-bit words per row
   int AW;               // words of the per-row activity mask = ceil(W / 32)
   int S, logS;          // lanes per row (power of two <= 32)
-  int TR;               // K2 tile height in rows
-  int TRa;              // K2 tile height for word-aligned rows (0: not used)
+  int TR;               // K2 tile height in rows (rows not word-aligned)
   int logP;             // K2 threads per row = 1 << logP (TR << logP == block size)
   int S3, logS3;        // K3 lanes per row (<= 8: several rows per warp)
 };
@@ -377,6 +396,7 @@ struct FeDims {
 // Per-isovalue workspace views.
 struct FeIsoWs {
   uint32_t* bits;       // flat node bitmask
+  uint2* sums;          // per 32 words of bits: {mixed, ones} (see K1)
   int* cnt;             // [R][4] row counts X, Y, Z, T
   uint32_t* wact;       // [R][AW] words of each row with any output (bitmask)
   long long* tot;       // [4] this slab's own totals (contiguous across isovalues)
@@ -676,74 +696,78 @@ k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nword
     count_rows<false>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
 }
 
-// K2a for rows that start on a word (L % 32 == 0): one thread per row.
-//
-// The tile's bit rows [R0, R0+TR] and [R0+M, R0+M+TR] are copied with
-// 4-byte cp.async into shared memory rows of SW = W+1 words (odd stride,
-// a zero word after each row).  Thread t counts row R0+t word by word; the
-// 32 lanes of a warp are 32 consecutive rows at the same word index, so they
-// read distinct banks, and since the surface is spatially coherent most
-// words are free of side changes in all 32 rows at once and cost a warp
-// only the loads and one vote.
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
-  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(sa), "l"(gmem) : "memory");
+// K2a for rows that start on a word (L % 32 == 0), driven by K1's word
+// summaries: one thread per node row.  For each group of 32 words of its row
+// the thread reads the {mixed, ones} summaries of the four rows around its
+// cells (8 bytes each) and forms the candidate words: a word can hold a
+// crossing or a cut cell only if one of the four rows is mixed there or at
+// the next word, or the rows' uniform values differ there or at the next
+// word, or row a's uniform value changes at the next word.  Only candidates
+// are loaded from the bitmask and counted exactly as the reference counts
+// them; on a smooth surface they are a few percent of all words.
+
+// Summary bits of flat words [f, f + 33) (the 33rd is word f + 32).
+__device__ __forceinline__ void sum_window(const uint2* __restrict__ s, int64_t f,
+                                           uint64_t* mixed, uint64_t* ones) {
+  const int64_t c = f >> 5;
+  const int o = (int)(f & 31);
+  const uint2 lo = __ldg(s + c), hi = __ldg(s + c + 1);
+  *mixed = (((((uint64_t)hi.x) << 32) | lo.x) >> o) & 0x1ffffffffull;
+  *ones = (((((uint64_t)hi.y) << 32) | lo.y) >> o) & 0x1ffffffffull;
 }
 
 __global__ void __launch_bounds__(kThreads)
-k_fe_count_aligned(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
-  extern __shared__ uint32_t k2_smem[];
+k_fe_count_sparse(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   __shared__ int s_ntri[256];
   const FeIsoWs& Wk = ws.iso[blockIdx.y];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = blockDim.x >> 5;
-  const int TR = d.TRa, W = d.W, SW = d.W + 1, AW = d.AW;
-  uint32_t* sA = k2_smem;                // (TR+1) rows of SW words
-  uint32_t* sC = k2_smem + (TR + 1) * SW;
-  for (int i = tid; i < 256; i += blockDim.x) s_ntri[i] = (int)(c_case_tris[i] >> 60);
-  const int64_t R0 = (int64_t)blockIdx.x * TR;
-  for (int rl = warp; rl <= TR; rl += nwarp) {
-    const int64_t ra = R0 + rl, rc = R0 + d.M + rl;
-    uint32_t* da = sA + rl * SW;
-    uint32_t* dc = sC + rl * SW;
-    for (int w = lane; w < W; w += 32) {
-      if (ra < d.R) cp_async4(da + w, Wk.bits + ra * W + w);
-      if (rc < d.R) cp_async4(dc + w, Wk.bits + rc * W + w);
-    }
-    if (lane == 0) {
-      da[W] = 0u;
-      dc[W] = 0u;
-    }
-  }
-  cp_async_wait_all();
+  s_ntri[threadIdx.x] = (int)(c_case_tris[threadIdx.x] >> 60);  // kThreads == 256
   __syncthreads();
-
-  const int64_t r = R0 + tid;
-  const bool valid = tid < TR && r < d.R;
+  const int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x;
+  if (r >= d.R) return;  // nothing warp-collective below
   const uint32_t M32 = (uint32_t)d.M;
-  const uint32_t j = valid ? (uint32_t)r % M32 : 0u, k = valid ? (uint32_t)r / M32 : 0u;
-  const bool hasY = valid && (j + 1 < M32);
-  const bool hasZ = valid && ((int64_t)k + 1 < d.N);
+  const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
+  const bool hasY = j + 1 < M32;
+  const bool hasZ = (int64_t)k + 1 < d.N;
   const bool hasC = hasY && hasZ;
-  const uint32_t* pa = sA + (valid ? tid : 0) * SW;
-  const uint32_t* pb = pa + SW;
-  const uint32_t* pc = sC + (valid ? tid : 0) * SW;
-  const uint32_t* pd = pc + SW;
-  const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
+  const int W = d.W;
   const int Li = (int)d.L;
+  // First word of each of the four rows; a missing neighbour row reads as a
+  // copy of row a (b, c) or of row b (d), so it adds no crossings.
+  const int64_t fa = r * W;
+  const int64_t fb = hasY ? fa + W : fa;
+  const int64_t fc = hasZ ? fa + d.M * W : fa;
+  const int64_t fd = hasC ? fc + W : fb;
+  const uint32_t* __restrict__ bits = Wk.bits;
+  const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
   unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
-  uint32_t amask = 0;
-  for (int w = 0; w < W; ++w) {
-    const uint32_t a = valid ? pa[w] : 0u, an = valid ? (pa[w + 1] & 1u) : 0u;
-    uint32_t b = a, bn = an, c = a, cn = an, dd, dn;
-    if (hasY) { b = pb[w]; bn = pb[w + 1] & 1u; }
-    if (hasZ) { c = pc[w]; cn = pc[w + 1] & 1u; }
-    dd = b; dn = bn;
-    if (hasC) { dd = pd[w]; dn = pd[w + 1] & 1u; }
-    const uint32_t a1 = (a >> 1) | (an << 31);
-    const uint32_t uu = (a ^ b) | (a ^ c) | (a ^ dd);
-    const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
-    const bool busy = (uu | (a ^ a1) | (un << 31)) != 0u;
-    if (__any_sync(0xffffffffu, busy) && busy) {
+  for (int g = 0; g < d.AW; ++g) {
+    const int w0 = 32 * g;
+    const int nvalid = W - w0;  // words of the row in this group (>= 1)
+    const uint64_t vm = nvalid >= 32 ? 0xffffffffull : ((1ull << nvalid) - 1ull);
+    const uint64_t nm = nvalid - 1 >= 32 ? 0xffffffffull : ((1ull << (nvalid - 1)) - 1ull);
+    uint64_t ma, oa, mb, ob, mc, oc, md, od;
+    sum_window(Wk.sums, fa + w0, &ma, &oa);
+    sum_window(Wk.sums, fb + w0, &mb, &ob);
+    sum_window(Wk.sums, fc + w0, &mc, &oc);
+    sum_window(Wk.sums, fd + w0, &md, &od);
+    const uint64_t x = ma | mb | mc | md | (oa ^ ob) | (oa ^ oc) | (oa ^ od);
+    uint32_t cand = (uint32_t)((x | (((x >> 1) | (oa ^ (oa >> 1))) & nm)) & vm);
+    uint32_t amask = 0;
+    while (cand) {
+      const int wb = __ffs(cand) - 1;
+      cand &= cand - 1u;
+      const int w = w0 + wb;
+      const bool more = w + 1 < W;
+      const uint32_t a = __ldg(bits + fa + w), b = __ldg(bits + fb + w);
+      const uint32_t c = __ldg(bits + fc + w), dd = __ldg(bits + fd + w);
+      uint32_t an = 0, bn = 0, cn = 0, dn = 0;
+      if (more) {
+        an = __ldg(bits + fa + w + 1) & 1u;
+        bn = __ldg(bits + fb + w + 1) & 1u;
+        cn = __ldg(bits + fc + w + 1) & 1u;
+        dn = __ldg(bits + fd + w + 1) & 1u;
+      }
+      const uint32_t a1 = (a >> 1) | (an << 31);
       const uint32_t xm = low_mask(Li - 1 - 32 * w);
       const unsigned x0 = __popc((a ^ a1) & xm);
       const unsigned y0 = __popc(a ^ b);
@@ -753,7 +777,9 @@ k_fe_count_aligned(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
         const uint32_t b1 = (b >> 1) | (bn << 31), c1 = (c >> 1) | (cn << 31);
         const uint32_t d1 = (dd >> 1) | (dn << 31);
         t0 = tri_count_word(a, a1, b, b1, c, c1, dd, d1, xm);
-        if (mask) {  // masked cells emit nothing: take their triangles back out
+        if (mask && t0) {  // masked cells emit nothing: take their triangles back out
+          const uint32_t uu = (a ^ b) | (a ^ c) | (a ^ dd);
+          const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
           uint32_t act = (uu | (uu >> 1) | (un << 31) | (a ^ a1)) & xm;
           while (act) {
             const int bit = __ffs(act) - 1;
@@ -767,14 +793,11 @@ k_fe_count_aligned(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
       cY += y0;
       cZ += z0;
       cT += t0;
-      if (x0 | y0 | z0 | t0) amask |= 1u << (w & 31);
+      if (x0 | y0 | z0 | t0) amask |= 1u << wb;
     }
-    if ((w & 31) == 31 || w == W - 1) {
-      if (valid) Wk.wact[r * AW + (w >> 5)] = amask;
-      amask = 0;
-    }
+    Wk.wact[r * d.AW + g] = amask;
   }
-  if (valid) reinterpret_cast<int4*>(Wk.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
+  reinterpret_cast<int4*>(Wk.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
 }
 
 // K2b: single-pass (decoupled look-back) exclusive scan of the row counts
@@ -1779,10 +1802,9 @@ k_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive, uint32_t* 
 
 struct FeLayout {
   FeDims d;
-  size_t k2_smem;   // dynamic shared memory of the count kernel
-  size_t k2a_smem;  // ... of the word-aligned count kernel
-  int64_t V, nwords, bits_stride;
-  size_t off_bits, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
+  size_t k2_smem;   // dynamic shared memory of the count kernel (rows not word-aligned)
+  int64_t V, nwords, bits_stride, nchunks, sums_stride;
+  size_t off_bits, off_sums, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
   size_t reset_bytes;  // info + flags, zeroed before each scan
 };
@@ -1820,24 +1842,14 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   d.S3 = S < 8 ? S : 8;
   d.logS3 = logS < 3 ? logS : 3;
   f.k2_smem = (size_t)(2 * k2_stage_words((int)TR, d.W)) * 4;
-  // Word-aligned rows: one thread per row, two staged runs of TRa+1 rows of
-  // W+1 words within ~200 KiB of shared memory.
-  d.TRa = 0;
-  if ((d.L & 31) == 0) {
-    int64_t t = 25600 / (d.W + 1) - 1;
-    if (t > 256) t = 256;
-    t = (t / 32) * 32;
-    if (t >= 32) {
-      d.TRa = (int)t;
-      d.ctiles_a = (d.R + t - 1) / t;
-      f.k2a_smem = (size_t)(2 * (t + 1) * (d.W + 1)) * 4;
-    }
-  }
-  if (d.TRa == 0 && f.k2_smem > 200 * 1024) return false;  // rows longer than ~90k nodes
+  // Rows that are not word-aligned are staged whole in shared memory.
+  if ((d.L & 31) != 0 && f.k2_smem > 200 * 1024) return false;  // longer than ~90k nodes
   if (d.R > 0xffffffffLL) return false;  // worklist holds uint32 row ids
   f.V = d.L * d.M * d.N;
   f.nwords = (f.V + 31) / 32;
   f.bits_stride = (int64_t)align_up((size_t)(f.nwords + 8), 64);
+  f.nchunks = (f.V + 1023) / 1024;
+  f.sums_stride = (int64_t)align_up((size_t)(f.nchunks + 2), 32);
   size_t o = 0;
   f.off_info = o;   o = align_up(o + (size_t)niso * 16 * 8, 256);
   f.off_flags = o;  o = align_up(o + (size_t)niso * d.ntiles * 4, 256);
@@ -1851,6 +1863,7 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.off_rowoff = o; o = align_up(o + (size_t)niso * d.R * 4 * 8, 256);
   f.off_work = o;   o = align_up(o + (size_t)niso * d.R * 4, 256);
   f.off_bits = o;   o = align_up(o + (size_t)niso * f.bits_stride * 4, 256);
+  f.off_sums = o;   o = align_up(o + (size_t)niso * f.sums_stride * 8, 256);
   f.total = o;
   *out = f;
   return true;
@@ -1862,6 +1875,7 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
   for (int q = 0; q < niso; ++q) {
     FeIsoWs& w = a.iso[q];
     w.bits = reinterpret_cast<uint32_t*>(b + f.off_bits) + (size_t)q * f.bits_stride;
+    w.sums = reinterpret_cast<uint2*>(b + f.off_sums) + (size_t)q * f.sums_stride;
     w.rowoff = reinterpret_cast<long long*>(b + f.off_rowoff) + (size_t)q * f.d.R * 4;
     w.cnt = reinterpret_cast<int*>(b + f.off_cnt) + (size_t)q * f.d.R * 4;
     w.wact = reinterpret_cast<uint32_t*>(b + f.off_wact) + (size_t)q * f.d.R * f.d.AW;
@@ -2102,12 +2116,13 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   const int64_t nchunks = (f.V + 1023) / 1024;
   const int g = grid_for(nchunks, kThreads / 32, 8);
   uint32_t* bits0 = v.iso[0].bits;
+  uint2* sums0 = v.iso[0].sums;
   if (vec)
     k_fe_threshold_v4<<<g, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0, f.bits_stride,
-                                              f.nwords);
+                                              f.nwords, sums0, f.sums_stride);
   else
     k_fe_threshold_scalar<<<g, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0, f.bits_stride,
-                                                  f.nwords);
+                                                  f.nwords, sums0, f.sums_stride);
   TK_LAUNCHED();
   return TKMC_OK;
 }
@@ -2123,12 +2138,9 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   TK_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + f.off_info, 0, f.reset_bytes - f.off_info, st));
   const int64_t skip = g_skip_tile.exchange(-1);
-  if (f.d.TRa > 0) {
-    if (f.k2a_smem > 48 * 1024)
-      TK_CUDA(cudaFuncSetAttribute(k_fe_count_aligned,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)f.k2a_smem));
-    k_fe_count_aligned<<<dim3((unsigned)f.d.ctiles_a, (unsigned)niso), f.d.TRa, f.k2a_smem,
-                         st>>>(f.d, v, mask);
+  if ((f.d.L & 31) == 0) {
+    k_fe_count_sparse<<<dim3((unsigned)((f.d.R + kThreads - 1) / kThreads), (unsigned)niso),
+                        kThreads, 0, st>>>(f.d, v, mask);
   } else {
     if (f.k2_smem > 48 * 1024)
       TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
