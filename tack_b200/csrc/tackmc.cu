@@ -383,7 +383,7 @@ struct FeDims {
   int64_t R;            // node rows = M * N
   int64_t n_own_rows;   // rows this slab owns (R, or R - M with a ghost plane)
   int64_t nx, ny;       // cells per row, cell rows per plane (mask index)
-  int64_t ntiles;       // K2b scan tiles
+  int64_t ntiles;       // scan tiles (K2b: kScanRows rows; aligned rows: kThreads rows)
   int64_t ctiles;       // K2a count tiles (rows not word-aligned)
   int W;                // 32-bit words per row
   int AW;               // words of the per-row activity mask = ceil(W / 32)
@@ -391,6 +391,15 @@ struct FeDims {
   int TR;               // K2 tile height in rows (rows not word-aligned)
   int logP;             // K2 threads per row = 1 << logP (TR << logP == block size)
   int S3, logS3;        // K3 lanes per row (<= 8: several rows per warp)
+};
+
+// One word of a node row with any output (word-aligned rows): the offsets,
+// relative to their sections, of its first x, y and z point and of its
+// first triangle.
+struct FeUnit {
+  uint32_t r, w;
+  uint32_t xo, yo, zo, pad;
+  long long to;
 };
 
 // Per-isovalue workspace views.
@@ -402,11 +411,15 @@ struct FeIsoWs {
   long long* tot;       // [4] this slab's own totals (contiguous across isovalues)
   long long* rowoff;    // [R][4] exclusive offsets X, Y, Z, T (section-relative)
   uint32_t* work;       // active own rows
+  uint32_t* ufirst;     // [R] index of each row's first unit (word-aligned rows)
+  uint32_t* ucnt;       // [R] units of each row (word-aligned rows)
+  uint2* uslot;         // [R][kUnitSlots] {word, packed counts} of a row's first units
+  FeUnit* units;        // units in (row, word) order, then a sentinel with the totals
   uint32_t* flags;      // [ntiles] (scan tiles of kScanRows rows)
   long long* agg;       // [ntiles][4]
   long long* incl;      // [ntiles][4]
   long long* info;      // [16]: 0-3 own totals, 4-7 all-row totals, 8 active rows,
-                        //       9 tile counter, 10 error
+                        //       9 tile counter, 10 error, 11 units, 12 own units
 };
 
 struct FeWsAll {
@@ -696,15 +709,40 @@ k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nword
     count_rows<false>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
 }
 
-// K2a for rows that start on a word (L % 32 == 0), driven by K1's word
-// summaries: one thread per node row.  For each group of 32 words of its row
-// the thread reads the {mixed, ones} summaries of the four rows around its
+// Position of the k-th (0-based) set bit of m; k < popc(m).
+__device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
+  int pos = 0;
+#pragma unroll
+  for (int sft = 16; sft >= 1; sft >>= 1) {
+    const int low = __popc(m & ((1u << sft) - 1u));
+    if (k >= low) {
+      k -= low;
+      m >>= sft;
+      pos += sft;
+    }
+  }
+  return pos;
+}
+
+// Word-aligned rows (L % 32 == 0): counts, offsets and the unit list.
+//
+// One thread per node row.  For each group of 32 words of its row the
+// thread reads K1's {mixed, ones} summaries of the four rows around its
 // cells (8 bytes each) and forms the candidate words: a word can hold a
 // crossing or a cut cell only if one of the four rows is mixed there or at
 // the next word, or the rows' uniform values differ there or at the next
 // word, or row a's uniform value changes at the next word.  Only candidates
 // are loaded from the bitmask and counted exactly as the reference counts
 // them; on a smooth surface they are a few percent of all words.
+//
+// A word with any output (own x/y/z crossings or triangles) is a "unit".
+// Three launches with no waiting between blocks: K2a counts (rows, words,
+// units) and leaves per-tile totals, K2b scans the tiles' totals, K2c writes
+// each row's offsets, the index of its first unit, and one FeUnit per unit
+// holding the section-relative offsets of the word's first x, y, z point and
+// first triangle.  Units are in (row, word) order, so the first unit at or
+// after any (row, word) position carries the offsets a crossing there would
+// have; the emit kernel finds neighbour rows' offsets that way.
 
 // Summary bits of flat words [f, f + 33) (the 33rd is word f + 32).
 __device__ __forceinline__ void sum_window(const uint2* __restrict__ s, int64_t f,
@@ -716,88 +754,391 @@ __device__ __forceinline__ void sum_window(const uint2* __restrict__ s, int64_t 
   *ones = (((((uint64_t)hi.y) << 32) | lo.y) >> o) & 0x1ffffffffull;
 }
 
-__global__ void __launch_bounds__(kThreads)
-k_fe_count_sparse(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
-  __shared__ int s_ntri[256];
-  const FeIsoWs& Wk = ws.iso[blockIdx.y];
-  s_ntri[threadIdx.x] = (int)(c_case_tris[threadIdx.x] >> 60);  // kThreads == 256
-  __syncthreads();
-  const int64_t r = (int64_t)blockIdx.x * kThreads + threadIdx.x;
-  if (r >= d.R) return;  // nothing warp-collective below
+// First flat words of the four rows around node row r (aligned rows).  A
+// missing neighbour row reads as a copy of row a (b, c) or of row b (d), so
+// it adds no crossings.
+struct RowQuad {
+  int64_t fa, fb, fc, fd;
+  uint32_t j, k;
+  bool hasY, hasZ, hasC;
+};
+
+__device__ __forceinline__ RowQuad row_quad(const FeDims& d, int64_t r) {
+  RowQuad q;
   const uint32_t M32 = (uint32_t)d.M;
-  const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
-  const bool hasY = j + 1 < M32;
-  const bool hasZ = (int64_t)k + 1 < d.N;
-  const bool hasC = hasY && hasZ;
-  const int W = d.W;
-  const int Li = (int)d.L;
-  // First word of each of the four rows; a missing neighbour row reads as a
-  // copy of row a (b, c) or of row b (d), so it adds no crossings.
-  const int64_t fa = r * W;
-  const int64_t fb = hasY ? fa + W : fa;
-  const int64_t fc = hasZ ? fa + d.M * W : fa;
-  const int64_t fd = hasC ? fc + W : fb;
-  const uint32_t* __restrict__ bits = Wk.bits;
-  const int64_t cell_row0 = ((int64_t)k * d.ny + j) * d.nx;
-  unsigned cX = 0, cY = 0, cZ = 0, cT = 0;
-  for (int g = 0; g < d.AW; ++g) {
-    const int w0 = 32 * g;
-    const int nvalid = W - w0;  // words of the row in this group (>= 1)
-    const uint64_t vm = nvalid >= 32 ? 0xffffffffull : ((1ull << nvalid) - 1ull);
-    const uint64_t nm = nvalid - 1 >= 32 ? 0xffffffffull : ((1ull << (nvalid - 1)) - 1ull);
-    uint64_t ma, oa, mb, ob, mc, oc, md, od;
-    sum_window(Wk.sums, fa + w0, &ma, &oa);
-    sum_window(Wk.sums, fb + w0, &mb, &ob);
-    sum_window(Wk.sums, fc + w0, &mc, &oc);
-    sum_window(Wk.sums, fd + w0, &md, &od);
-    const uint64_t x = ma | mb | mc | md | (oa ^ ob) | (oa ^ oc) | (oa ^ od);
-    uint32_t cand = (uint32_t)((x | (((x >> 1) | (oa ^ (oa >> 1))) & nm)) & vm);
-    uint32_t amask = 0;
-    while (cand) {
-      const int wb = __ffs(cand) - 1;
-      cand &= cand - 1u;
-      const int w = w0 + wb;
-      const bool more = w + 1 < W;
-      const uint32_t a = __ldg(bits + fa + w), b = __ldg(bits + fb + w);
-      const uint32_t c = __ldg(bits + fc + w), dd = __ldg(bits + fd + w);
-      uint32_t an = 0, bn = 0, cn = 0, dn = 0;
-      if (more) {
-        an = __ldg(bits + fa + w + 1) & 1u;
-        bn = __ldg(bits + fb + w + 1) & 1u;
-        cn = __ldg(bits + fc + w + 1) & 1u;
-        dn = __ldg(bits + fd + w + 1) & 1u;
+  q.j = (uint32_t)r % M32;
+  q.k = (uint32_t)r / M32;
+  q.hasY = q.j + 1 < M32;
+  q.hasZ = (int64_t)q.k + 1 < d.N;
+  q.hasC = q.hasY && q.hasZ;
+  q.fa = r * d.W;
+  q.fb = q.hasY ? q.fa + d.W : q.fa;
+  q.fc = q.hasZ ? q.fa + d.M * d.W : q.fa;
+  q.fd = q.hasC ? q.fc + d.W : q.fb;
+  return q;
+}
+
+// Candidate words of group g (words 32g .. 32g+31) of the row.
+__device__ __forceinline__ uint32_t candidates(const uint2* __restrict__ sums, const RowQuad& q,
+                                               int W, int g) {
+  const int w0 = 32 * g;
+  const int nvalid = W - w0;  // words of the row in this group (>= 1)
+  const uint64_t vm = nvalid >= 32 ? 0xffffffffull : ((1ull << nvalid) - 1ull);
+  const uint64_t nm = nvalid - 1 >= 32 ? 0xffffffffull : ((1ull << (nvalid - 1)) - 1ull);
+  uint64_t ma, oa, mb, ob, mc, oc, md, od;
+  sum_window(sums, q.fa + w0, &ma, &oa);
+  sum_window(sums, q.fb + w0, &mb, &ob);
+  sum_window(sums, q.fc + w0, &mc, &oc);
+  sum_window(sums, q.fd + w0, &md, &od);
+  const uint64_t x = ma | mb | mc | md | (oa ^ ob) | (oa ^ oc) | (oa ^ od);
+  return (uint32_t)((x | (((x >> 1) | (oa ^ (oa >> 1))) & nm)) & vm);
+}
+
+// The bit words of the four rows at word w, and bit 0 of word w + 1 (zero
+// past the row's end).
+struct WordQuad {
+  uint32_t a, b, c, d, an, bn, cn, dn;
+};
+
+__device__ __forceinline__ WordQuad load_word_quad(const uint32_t* __restrict__ bits,
+                                                   const RowQuad& q, int w, int W) {
+  WordQuad x;
+  x.a = __ldg(bits + q.fa + w);
+  x.b = __ldg(bits + q.fb + w);
+  x.c = __ldg(bits + q.fc + w);
+  x.d = __ldg(bits + q.fd + w);
+  x.an = x.bn = x.cn = x.dn = 0u;
+  if (w + 1 < W) {
+    x.an = __ldg(bits + q.fa + w + 1) & 1u;
+    x.bn = __ldg(bits + q.fb + w + 1) & 1u;
+    x.cn = __ldg(bits + q.fc + w + 1) & 1u;
+    x.dn = __ldg(bits + q.fd + w + 1) & 1u;
+  }
+  return x;
+}
+
+// Exact counts of word w: own x, y, z crossings and triangles of its cells
+// (masked cells emit none), packed as x | y << 6 | z << 12 | t << 18.
+__device__ __forceinline__ uint32_t count_word(const WordQuad& x, const RowQuad& q, int w, int Li,
+                                               const FeDims& d, const int32_t* __restrict__ mask,
+                                               const int* s_ntri) {
+  const uint32_t a1 = (x.a >> 1) | (x.an << 31);
+  const uint32_t xm = low_mask(Li - 1 - 32 * w);
+  const unsigned x0 = __popc((x.a ^ a1) & xm);
+  const unsigned y0 = __popc(x.a ^ x.b);
+  const unsigned z0 = __popc(x.a ^ x.c);
+  unsigned t0 = 0;
+  if (q.hasC) {
+    const uint32_t b1 = (x.b >> 1) | (x.bn << 31), c1 = (x.c >> 1) | (x.cn << 31);
+    const uint32_t d1 = (x.d >> 1) | (x.dn << 31);
+    t0 = tri_count_word(x.a, a1, x.b, b1, x.c, c1, x.d, d1, xm);
+    if (mask && t0) {  // masked cells emit nothing: take their triangles back out
+      const int64_t cell_row0 = ((int64_t)q.k * d.ny + q.j) * d.nx;
+      const uint32_t uu = (x.a ^ x.b) | (x.a ^ x.c) | (x.a ^ x.d);
+      const uint32_t un = (x.an ^ x.bn) | (x.an ^ x.cn) | (x.an ^ x.dn);
+      uint32_t act = (uu | (uu >> 1) | (un << 31) | (x.a ^ a1)) & xm;
+      while (act) {
+        const int bit = __ffs(act) - 1;
+        act &= act - 1;
+        if (__ldg(mask + cell_row0 + 32 * w + bit) != 0)
+          t0 -= (unsigned)s_ntri[cell_case(bit, x.a, a1, x.b, b1, x.c, c1, x.d, d1)];
       }
-      const uint32_t a1 = (a >> 1) | (an << 31);
-      const uint32_t xm = low_mask(Li - 1 - 32 * w);
-      const unsigned x0 = __popc((a ^ a1) & xm);
-      const unsigned y0 = __popc(a ^ b);
-      const unsigned z0 = __popc(a ^ c);
-      unsigned t0 = 0;
-      if (hasC) {
-        const uint32_t b1 = (b >> 1) | (bn << 31), c1 = (c >> 1) | (cn << 31);
-        const uint32_t d1 = (dd >> 1) | (dn << 31);
-        t0 = tri_count_word(a, a1, b, b1, c, c1, dd, d1, xm);
-        if (mask && t0) {  // masked cells emit nothing: take their triangles back out
-          const uint32_t uu = (a ^ b) | (a ^ c) | (a ^ dd);
-          const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
-          uint32_t act = (uu | (uu >> 1) | (un << 31) | (a ^ a1)) & xm;
+    }
+  }
+  return x0 | (y0 << 6) | (z0 << 12) | (t0 << 18);
+}
+
+constexpr int kUnitSlots = 8;  // units per row remembered between the count and offsets passes
+
+__device__ __forceinline__ void put_unit(FeUnit* units, int64_t cap, int64_t ui, uint32_t r,
+                                         uint32_t w, const long long (&o)[4]) {
+  if (ui >= cap) return;  // the emit falls back to the row-wise kernel
+  uint4* p = reinterpret_cast<uint4*>(units + ui);
+  p[0] = make_uint4(r, w, (uint32_t)o[0], (uint32_t)o[1]);
+  p[1] = make_uint4((uint32_t)o[2], 0u, (uint32_t)(unsigned long long)o[3],
+                    (uint32_t)((unsigned long long)o[3] >> 32));
+}
+
+// Largest lane l whose (non-decreasing across lanes) value v_l is <= e.
+__device__ __forceinline__ int owner_lane(unsigned v, unsigned e) {
+  int lo = 0;
+#pragma unroll
+  for (int step = 16; step >= 1; step >>= 1) {
+    const unsigned vm = __shfl_sync(0xffffffffu, v, lo + step < 32 ? lo + step : 31);
+    if (lo + step < 32 && vm <= e) lo += step;
+  }
+  return lo;
+}
+
+// Lanes below `lane` in the run of equal keys that contains it (runs of a
+// key are contiguous).
+__device__ __forceinline__ uint32_t run_below_mask(int key) {
+  const int lane = threadIdx.x & 31;
+  const int prev = __shfl_up_sync(0xffffffffu, key, 1);
+  const bool head = lane == 0 || prev != key;
+  const uint32_t hm = __ballot_sync(0xffffffffu, head);
+  const uint32_t upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
+  const int first = 31 - __clz(hm & upto);
+  return ((1u << lane) - 1u) & ~((1u << first) - 1u);
+}
+
+// K2a (word-aligned rows): per-row counts, activity masks and unit slots.
+// A warp owns 32 consecutive node rows.  Lane = row finds the row's
+// candidate words; the warp then lists all candidates of its rows and counts
+// them 32 at a time, lane = candidate, so that the bit loads of 32 words are
+// in flight together.  Per-row sums go through shared-memory atomics; the
+// first kUnitSlots active words of each row are remembered (word index and
+// packed counts) for the offsets pass.  Each block also leaves its tile's
+// totals {X, Y, Z, T, units} for the tile scan.
+__global__ void __launch_bounds__(kThreads)
+k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
+  __shared__ int s_ntri[256];
+  __shared__ unsigned s_cnt[4][kThreads];
+  __shared__ unsigned s_nu[kThreads];
+  __shared__ uint32_t s_act[kThreads];
+  __shared__ long long s_red[5][kThreads / 32];
+  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256
+#pragma unroll
+  for (int t = 0; t < 4; ++t) s_cnt[t][tid] = 0;
+  s_nu[tid] = 0;
+  __syncthreads();
+  const int64_t rbase = (int64_t)blockIdx.x * kThreads + warp * 32;  // the warp's first row
+  const int64_t r = rbase + lane;
+  const bool valid = r < d.R;
+  const int W = d.W, Li = (int)d.L;
+  RowQuad q{};
+  if (valid) q = row_quad(d, r);
+  for (int g = 0; g < d.AW; ++g) {
+    const uint32_t cand = valid ? candidates(Wk.sums, q, W, g) : 0u;
+    s_act[tid] = 0u;
+    const unsigned nc = __popc(cand);
+    unsigned pre = nc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, pre, o);
+      if (lane >= o) pre += y;
+    }
+    const unsigned NC = __shfl_sync(0xffffffffu, pre, 31);
+    pre -= nc;
+    __syncwarp();
+    for (unsigned b0 = 0; b0 < NC; b0 += 32) {
+      const unsigned e = b0 + lane;
+      const bool ve = e < NC;
+      const int own = owner_lane(pre, ve ? e : NC - 1);
+      const uint32_t ocand = __shfl_sync(0xffffffffu, cand, own);
+      const unsigned opre = __shfl_sync(0xffffffffu, pre, own);
+      uint32_t c = 0u;
+      int w = 0;
+      if (ve) {
+        const int wb = nth_set_bit(ocand, (int)(e - opre));
+        w = 32 * g + wb;
+        const RowQuad oq = row_quad(d, rbase + own);
+        c = count_word(load_word_quad(Wk.bits, oq, w, W), oq, w, Li, d, mask, s_ntri);
+      }
+      const bool active = c != 0u;
+      const int rl = warp * 32 + own;
+      if (active) {
+        atomicAdd(&s_cnt[0][rl], c & 63u);
+        atomicAdd(&s_cnt[1][rl], (c >> 6) & 63u);
+        atomicAdd(&s_cnt[2][rl], (c >> 12) & 63u);
+        atomicAdd(&s_cnt[3][rl], c >> 18);
+        atomicOr(&s_act[rl], 1u << (w & 31));
+      }
+      const uint32_t ab = __ballot_sync(0xffffffffu, active);
+      const uint32_t below = run_below_mask(ve ? own : -1);
+      const unsigned slot = s_nu[rl] + __popc(ab & below);
+      __syncwarp();
+      if (active) {
+        if (slot < kUnitSlots)
+          Wk.uslot[(rbase + own) * kUnitSlots + slot] = make_uint2((uint32_t)w, c);
+        atomicAdd(&s_nu[rl], 1u);
+      }
+      __syncwarp();
+    }
+    if (valid) Wk.wact[r * d.AW + g] = s_act[tid];
+    __syncwarp();
+  }
+  long long own5[5] = {0, 0, 0, 0, 0};
+  if (valid) {
+    reinterpret_cast<int4*>(Wk.cnt)[r] =
+        make_int4((int)s_cnt[0][tid], (int)s_cnt[1][tid], (int)s_cnt[2][tid], (int)s_cnt[3][tid]);
+    Wk.ucnt[r] = s_nu[tid];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) own5[t] = s_cnt[t][tid];
+    own5[4] = s_nu[tid];
+  }
+#pragma unroll
+  for (int t = 0; t < 5; ++t) {
+    long long x = own5[t];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == 0) s_red[t][warp] = x;
+  }
+  __syncthreads();
+  if (tid < 5) {
+    long long x = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < kThreads / 32; ++w2) x += s_red[tid][w2];
+    Wk.agg[blockIdx.x * 5 + tid] = x;
+  }
+}
+
+// K2b (word-aligned rows): exclusive scan of the tiles' totals by one block
+// per isovalue (the tiles are few: one per 256 rows) into incl[tile], the
+// all-row totals, and the sentinel unit after the last one.
+__global__ void __launch_bounds__(1024)
+k_fe_scan_tiles(FeDims d, FeWsAll ws, int64_t unit_cap) {
+  __shared__ long long s_w[5][32];
+  __shared__ long long s_carry[5];
+  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid < 5) s_carry[tid] = 0;
+  __syncthreads();
+  for (int64_t t0 = 0; t0 < d.ntiles; t0 += 1024) {
+    const int64_t t = t0 + tid;
+    long long v[5], inc[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      v[k] = t < d.ntiles ? Wk.agg[t * 5 + k] : 0;
+      long long x = v[k];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      inc[k] = x;
+      if (lane == 31) s_w[k][warp] = x;
+    }
+    __syncthreads();
+    long long total[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      long long before = 0, all = 0;
+      for (int w2 = 0; w2 < 32; ++w2) {
+        const long long x = s_w[k][w2];
+        if (w2 < warp) before += x;
+        all += x;
+      }
+      if (t < d.ntiles) Wk.incl[t * 5 + k] = s_carry[k] + before + inc[k] - v[k];
+      total[k] = all;
+    }
+    __syncthreads();
+    if (tid < 5) s_carry[tid] += total[tid];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    long long all[5];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) all[k] = s_carry[k];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) Wk.info[4 + k] = all[k];
+    Wk.info[11] = all[4];
+    if (d.n_own_rows == d.R) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) Wk.info[k] = Wk.tot[k] = all[k];
+      Wk.info[12] = all[4];
+    }
+    // Sentinel after the last unit: the totals, for lookups past the end.
+    const long long o[4] = {all[0], all[1], all[2], all[3]};
+    put_unit(Wk.units, unit_cap, all[4], (uint32_t)d.R, 0u, o);
+  }
+}
+
+// K2c (word-aligned rows): row offsets, first unit of each row, the units,
+// own totals and the worklist of active own rows.  One thread per row; the
+// tile's prefix comes from the tile scan.
+__global__ void __launch_bounds__(kThreads)
+k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t unit_cap) {
+  __shared__ int s_ntri[256];
+  __shared__ long long s_w[5][kThreads / 32];
+  __shared__ unsigned s_wbase[kThreads / 32];
+  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256; synced below
+  const int64_t tile = blockIdx.x;
+  const int64_t r = tile * kThreads + tid;
+  const bool valid = r < d.R;
+  int4 c = make_int4(0, 0, 0, 0);
+  unsigned nU = 0;
+  if (valid) {
+    c = __ldcg(reinterpret_cast<const int4*>(Wk.cnt) + r);
+    nU = __ldcg(Wk.ucnt + r);
+  }
+  const long long own[5] = {c.x, c.y, c.z, c.w, nU};
+  long long inc[5];
+#pragma unroll
+  for (int t = 0; t < 5; ++t) {
+    long long x = own[t];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    inc[t] = x;
+    if (lane == 31) s_w[t][warp] = x;
+  }
+  __syncthreads();
+  long long ex[5];
+#pragma unroll
+  for (int t = 0; t < 5; ++t) {
+    long long before = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < kThreads / 32; ++w2)
+      if (w2 < warp) before += s_w[t][w2];
+    ex[t] = __ldcg(Wk.incl + tile * 5 + t) + before + inc[t] - own[t];
+  }
+  if (valid) {
+    longlong2* dst = reinterpret_cast<longlong2*>(Wk.rowoff + r * 4);
+    dst[0] = make_longlong2(ex[0], ex[1]);
+    dst[1] = make_longlong2(ex[2], ex[3]);
+    Wk.ufirst[r] = (uint32_t)ex[4];
+    // Own totals: the offsets of the first ghost row.
+    if (r == d.n_own_rows) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t) Wk.info[t] = Wk.tot[t] = ex[t];
+      Wk.info[12] = ex[4];
+    }
+    if (nU) {
+      long long o[4] = {ex[0], ex[1], ex[2], ex[3]};
+      int64_t ui = ex[4];
+      if (nU <= kUnitSlots) {
+        for (unsigned i = 0; i < nU; ++i) {
+          const uint2 sl = __ldcg(Wk.uslot + r * kUnitSlots + i);
+          put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, sl.x, o);
+          o[0] += sl.y & 63u;
+          o[1] += (sl.y >> 6) & 63u;
+          o[2] += (sl.y >> 12) & 63u;
+          o[3] += sl.y >> 18;
+        }
+      } else {  // long active rows: count their active words again
+        const RowQuad q = row_quad(d, r);
+        for (int g = 0; g < d.AW; ++g) {
+          uint32_t act = __ldcg(Wk.wact + r * d.AW + g);
           while (act) {
-            const int bit = __ffs(act) - 1;
-            act &= act - 1;
-            if (__ldg(mask + cell_row0 + 32 * w + bit) != 0)
-              t0 -= (unsigned)s_ntri[cell_case(bit, a, a1, b, b1, c, c1, dd, d1)];
+            const int w = 32 * g + __ffs(act) - 1;
+            act &= act - 1u;
+            const uint32_t cw = count_word(load_word_quad(Wk.bits, q, w, d.W), q, w, (int)d.L,
+                                           d, mask, s_ntri);
+            put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, (uint32_t)w, o);
+            o[0] += cw & 63u;
+            o[1] += (cw >> 6) & 63u;
+            o[2] += (cw >> 12) & 63u;
+            o[3] += cw >> 18;
           }
         }
       }
-      cX += x0;
-      cY += y0;
-      cZ += z0;
-      cT += t0;
-      if (x0 | y0 | z0 | t0) amask |= 1u << wb;
     }
-    Wk.wact[r * d.AW + g] = amask;
   }
-  reinterpret_cast<int4*>(Wk.cnt)[r] = make_int4((int)cX, (int)cY, (int)cZ, (int)cT);
+  // Worklist of own rows with any output, for the row-wise emit kernel.
+  const bool act_row = valid && r < d.n_own_rows && nU != 0;
+  const uint32_t bal = __ballot_sync(0xffffffffu, act_row);
+  if (lane == 0 && bal)
+    s_wbase[warp] = (unsigned)atomicAdd((unsigned long long*)(Wk.info + 8),
+                                        (unsigned long long)__popc(bal));
+  __syncwarp();
+  if (act_row) Wk.work[s_wbase[warp] + __popc(bal & ((1u << lane) - 1u))] = (uint32_t)r;
 }
 
 // K2b: single-pass (decoupled look-back) exclusive scan of the row counts
@@ -977,20 +1318,6 @@ __device__ __forceinline__ void rec_put_i64(uint32_t* rec, int at, long long v) 
   rec[at + 1] = (uint32_t)((unsigned long long)v >> 32);
 }
 
-// Position of the k-th (0-based) set bit of m; k < popc(m).
-__device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
-  int pos = 0;
-#pragma unroll
-  for (int sft = 16; sft >= 1; sft >>= 1) {
-    const int low = __popc(m & ((1u << sft) - 1u));
-    if (k >= low) {
-      k -= low;
-      m >>= sft;
-      pos += sft;
-    }
-  }
-  return pos;
-}
 
 // Largest word u of the warp whose record field `field` (non-decreasing in u)
 // is <= e.
@@ -1352,12 +1679,14 @@ __device__ __forceinline__ uint32_t row_word_next(const uint32_t* __restrict__ b
 }
 
 __global__ void __launch_bounds__(kThreads, 3)
-k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
+k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
   extern __shared__ uint32_t k3_smem[];
   __shared__ uint64_t s_case[256];
   EmitSmem& S = *reinterpret_cast<EmitSmem*>(k3_smem);
   const int isoi = blockIdx.y;
   const FeIsoWs& W = ws.iso[isoi];
+  // Word-aligned rows whose unit list fit are emitted by k_fe_emit_units.
+  if (unit_cap > 0 && *((volatile long long*)(W.info + 11)) + 1 <= unit_cap) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_tris[tid];
   __syncthreads();
@@ -1639,6 +1968,249 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
 }
 
 // ------------------------------------------------------------------------
+// K3 for word-aligned rows: units, then points, then triangles, 32 at a time
+// ------------------------------------------------------------------------
+//
+// A unit is one word of an own node row with output (see K2a-K2c).  A warp
+// takes 32 consecutive units.  Lane = unit: load the unit, the four rows'
+// bit words, the eight crossing masks around its cells, and the offsets of
+// the eight edge groups: the unit's own x/y/z offsets and those of the first
+// unit at or after word w of rows b, c and d (the unit order makes that the
+// offset of word w's first crossing there).  Then lane = point over all the
+// units' own crossings (two volume reads each, the reference's arithmetic),
+// and lane = cell over all their cut cells (case from the bits, triangle
+// slots by a per-unit segmented prefix, ids = group offset + rank of the
+// crossing in its word).
+
+// Index of the first unit of node row `row` at word >= w.
+__device__ __forceinline__ int64_t unit_at(const FeIsoWs& W, const FeDims& d, int64_t row, int w) {
+  int64_t u = __ldg(W.ufirst + row);
+  const uint32_t* act = W.wact + row * d.AW;
+  const int gw = w >> 5;
+  for (int i = 0; i < gw; ++i) u += __popc(__ldg(act + i));
+  return u + __popc(__ldg(act + gw) & ((1u << (w & 31)) - 1u));
+}
+
+// Shared record of one unit (32-bit words).
+constexpr int kUB = 0;     // 8 id offsets of the edge groups (id base included)
+constexpr int kUM = 8;     // 8 crossing masks
+constexpr int kUQ = 16;    // bit words a a1 b b1 c c1 d d1
+constexpr int kUAct = 24;  // cut cells of the word
+constexpr int kURow = 25, kUW = 26;  // node row, word
+constexpr int kUPP = 27;   // exclusive prefix of points over the warp's units
+constexpr int kUPC = 28;   // exclusive prefix of cut cells
+constexpr int kUS = 29;
+
+__device__ __forceinline__ int find_rec(const uint32_t* recs, int field, unsigned e) {
+  int lo = 0;
+#pragma unroll
+  for (int step = 16; step >= 1; step >>= 1)
+    if (recs[(lo + step) * kUS + field] <= e) lo += step;
+  return lo;
+}
+
+__global__ void __launch_bounds__(kThreads)
+k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
+  __shared__ uint64_t s_case[256];
+  __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
+  __shared__ long long s_tri[kThreads / 32][32];
+  const int isoi = blockIdx.y;
+  const FeIsoWs& W = ws.iso[isoi];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_case[tid] = c_case_tris[tid];  // kThreads == 256
+  __syncthreads();
+  const long long n_all = *((volatile long long*)(W.info + 11));
+  if (n_all + 1 > unit_cap) return;  // the unit list overflowed: k_fe_emit_words runs instead
+  const long long n_own = *((volatile long long*)(W.info + 12));
+  uint32_t* U = s_rec[warp];
+  long long* TR = s_tri[warp];
+  const int Wd = d.W, Li = (int)d.L;
+  const int64_t L = d.L, plane = d.L * d.M;
+  const uint32_t M32 = (uint32_t)d.M;
+  const float iso = A.iso.v[isoi];
+  const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
+  const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
+  const long long idX = A.pt_id_base[isoi][0], idY = A.pt_id_base[isoi][1],
+                  idZ = A.pt_id_base[isoi][2];
+  const long long shX = A.pt_out_base[isoi][0] - idX, shY = A.pt_out_base[isoi][1] - idY,
+                  shZ = A.pt_out_base[isoi][2] - idZ;
+  const long long outT = A.tri_out_base[isoi];
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t grp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5; grp * 32 < n_own;
+       grp += nwarps) {
+    // ---- lane = unit ----
+    const int64_t u = grp * 32 + lane;
+    unsigned np = 0, nc = 0;
+    uint32_t* rec = U + lane * kUS;
+    if (u < n_own) {
+      const uint4* up = reinterpret_cast<const uint4*>(W.units + u);
+      const uint4 u0 = __ldg(up), u1 = __ldg(up + 1);
+      const int64_t r = u0.x;
+      const int w = (int)u0.y;
+      const RowQuad q = row_quad(d, r);
+      const WordQuad x = load_word_quad(W.bits, q, w, Wd);
+      const uint32_t xm = low_mask(Li - 1 - 32 * w);
+      const uint32_t a1 = (x.a >> 1) | (x.an << 31), b1 = (x.b >> 1) | (x.bn << 31);
+      const uint32_t c1 = (x.c >> 1) | (x.cn << 31), d1 = (x.d >> 1) | (x.dn << 31);
+      const uint32_t m0 = (x.a ^ a1) & xm, m1 = x.a ^ x.b, m2 = x.a ^ x.c;
+      uint32_t act = 0;
+      uint32_t bx = 0, bz = 0, cx = 0, cy = 0, dx = 0;
+      if (q.hasC) {
+        const uint32_t uu = m1 | m2 | (x.a ^ x.d);
+        const uint32_t un = (x.an ^ x.bn) | (x.an ^ x.cn) | (x.an ^ x.dn);
+        act = (uu | (uu >> 1) | (un << 31) | m0) & xm;
+        if (act) {
+          const uint4* pb = reinterpret_cast<const uint4*>(W.units + unit_at(W, d, r + 1, w));
+          const uint4* pc = reinterpret_cast<const uint4*>(W.units + unit_at(W, d, r + d.M, w));
+          const uint4* pd =
+              reinterpret_cast<const uint4*>(W.units + unit_at(W, d, r + d.M + 1, w));
+          const uint4 b0 = __ldg(pb), b1r = __ldg(pb + 1), c0 = __ldg(pc), d0 = __ldg(pd);
+          bx = b0.z;
+          bz = b1r.x;
+          cx = c0.z;
+          cy = c0.w;
+          dx = d0.z;
+        }
+      }
+      rec[kUB + 0] = (uint32_t)(idX + u0.z);
+      rec[kUB + 1] = (uint32_t)(idY + u0.w);
+      rec[kUB + 2] = (uint32_t)(idZ + u1.x);
+      rec[kUB + 3] = (uint32_t)(idX + bx);
+      rec[kUB + 4] = (uint32_t)(idX + cx);
+      rec[kUB + 5] = (uint32_t)(idX + dx);
+      rec[kUB + 6] = (uint32_t)(idY + cy);
+      rec[kUB + 7] = (uint32_t)(idZ + bz);
+      rec[kUM + 0] = m0;
+      rec[kUM + 1] = m1;
+      rec[kUM + 2] = m2;
+      rec[kUM + 3] = (x.b ^ b1) & xm;
+      rec[kUM + 4] = (x.c ^ c1) & xm;
+      rec[kUM + 5] = (x.d ^ d1) & xm;
+      rec[kUM + 6] = x.c ^ x.d;
+      rec[kUM + 7] = x.b ^ x.d;
+      rec[kUQ + 0] = x.a; rec[kUQ + 1] = a1;
+      rec[kUQ + 2] = x.b; rec[kUQ + 3] = b1;
+      rec[kUQ + 4] = x.c; rec[kUQ + 5] = c1;
+      rec[kUQ + 6] = x.d; rec[kUQ + 7] = d1;
+      rec[kUAct] = act;
+      rec[kURow] = (uint32_t)r;
+      rec[kUW] = (uint32_t)w;
+      TR[lane] = outT + (long long)(((unsigned long long)u1.w << 32) | u1.z);
+      np = __popc(m0) + __popc(m1) + __popc(m2);
+      nc = __popc(act);
+    }
+    unsigned pc = np | (nc << 16);
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, pc, o);
+      if (lane >= o) pc += y;
+    }
+    const unsigned tot = __shfl_sync(0xffffffffu, pc, 31);
+    pc -= np | (nc << 16);
+    // Lanes past the last unit get prefixes no item reaches.
+    rec[kUPP] = u < n_own ? (pc & 0xffffu) : 0xffffffffu;
+    rec[kUPC] = u < n_own ? (pc >> 16) : 0xffffffffu;
+    const unsigned NP = tot & 0xffffu, NC = tot >> 16;
+    __syncwarp();
+
+    // ---- lane = point ----
+    for (unsigned p0 = 0; p0 < NP; p0 += 32) {
+      const unsigned pe = p0 + lane;
+      if (pe < NP) {
+        const uint32_t* R = U + find_rec(U, kUPP, pe) * kUS;
+        int kk = (int)(pe - R[kUPP]);
+        const uint32_t mx = R[kUM + 0], my = R[kUM + 1];
+        const int cxn = __popc(mx), cyn = __popc(my);
+        int type;
+        uint32_t mm;
+        if (kk < cxn) {
+          type = 0; mm = mx;
+        } else if (kk < cxn + cyn) {
+          type = 1; mm = my; kk -= cxn;
+        } else {
+          type = 2; mm = R[kUM + 2]; kk -= cxn + cyn;
+        }
+        const int bit = nth_set_bit(mm, kk);
+        const int64_t r = R[kURow];
+        const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
+        const int64_t n = 32 * (int64_t)R[kUW] + bit;
+        const int64_t node = r * L + n;
+        const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
+        const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
+        const long long row = (long long)R[kUB + type] + kk +
+                              (type == 0 ? shX : (type == 1 ? shY : shZ));
+        if (row < 0 || row >= A.points_cap) {
+          record_overflow(W.info);
+        } else {
+          const float t = interp_t(iso, s0, s1);
+          const float px = coord(x0, n, hx);
+          const float py = coord(y0, j, hy);
+          const float pz = coord(z0, (int64_t)k + A.k_offset, hz);
+          const float px1 = type == 0 ? coord(x0, n + 1, hx) : px;
+          const float py1 = type == 1 ? coord(y0, (int64_t)j + 1, hy) : py;
+          const float pz1 = type == 2 ? coord(z0, (int64_t)k + 1 + A.k_offset, hz) : pz;
+          float* o = A.points + row * 3;
+          o[0] = lerp_ref(px, px1, t);
+          o[1] = lerp_ref(py, py1, t);
+          o[2] = lerp_ref(pz, pz1, t);
+        }
+      }
+    }
+
+    // ---- lane = cut cell ----
+    for (unsigned c0 = 0; c0 < NC; c0 += 32) {
+      const unsigned ce = c0 + lane;
+      const bool vc = ce < NC;
+      int ui = -1, cb = 0;
+      unsigned nt = 0;
+      uint64_t pkc = 0;
+      if (vc) {
+        ui = find_rec(U, kUPC, ce);
+        const uint32_t* R = U + ui * kUS;
+        cb = nth_set_bit(R[kUAct], (int)(ce - R[kUPC]));
+        bool masked = false;
+        if (A.mask) {
+          const int64_t r = R[kURow];
+          const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
+          masked = __ldg(A.mask + ((int64_t)k * d.ny + j) * d.nx + 32 * (int64_t)R[kUW] + cb) != 0;
+        }
+        if (!masked) {
+          pkc = s_case[cell_case(cb, R[kUQ + 0], R[kUQ + 1], R[kUQ + 2], R[kUQ + 3], R[kUQ + 4],
+                                 R[kUQ + 5], R[kUQ + 6], R[kUQ + 7])];
+          nt = (unsigned)(pkc >> 60);
+        }
+      }
+      unsigned run_tot;
+      bool last;
+      const unsigned ex = seg_excl(nt, ui, &run_tot, &last);
+      const long long tb = vc ? TR[ui] : 0;
+      if (nt) {
+        const long long tpos = tb + ex;
+        if (tpos < 0 || tpos + nt > A.conn_cap) {
+          record_overflow(W.info);
+        } else {
+          const uint32_t* R = U + ui * kUS;
+          const uint32_t below = (1u << cb) - 1u;
+          const uint32_t below1 = cb == 31 ? 0xffffffffu : ((2u << cb) - 1u);
+          int32_t* o = A.conn + tpos * 3;
+          for (unsigned t = 0; t < 3 * nt; ++t) {
+            const unsigned ed = (unsigned)(pkc >> (4 * t)) & 0xfu;
+            const unsigned gp = (unsigned)(kEdgeGroup >> (4 * ed)) & 0xfu;
+            const unsigned g = gp & 7u;
+            const uint32_t lim = (gp & 8u) ? below1 : below;
+            o[t] = (int32_t)(R[kUB + g] + __popc(R[kUM + g] & lim));
+          }
+        }
+      }
+      __syncwarp();
+      if (vc && last) TR[ui] = tb + run_tot;
+      __syncwarp();
+    }
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------------------
 // per-cell classification (26_marching_cubes.py:435-450)
 // ------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads)
@@ -1804,6 +2376,8 @@ struct FeLayout {
   FeDims d;
   size_t k2_smem;   // dynamic shared memory of the count kernel (rows not word-aligned)
   int64_t V, nwords, bits_stride, nchunks, sums_stride;
+  int64_t unit_cap;  // units (incl. the sentinel) the workspace holds; 0: rows not word-aligned
+  size_t off_units, off_ufirst, off_ucnt, off_uslot;
   size_t off_bits, off_sums, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
   size_t reset_bytes;  // info + flags, zeroed before each scan
@@ -1838,7 +2412,8 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   d.TR = (int)TR;
   d.logP = 0;
   d.ctiles = (d.R + TR - 1) / TR;
-  d.ntiles = (d.R + kScanRows - 1) / kScanRows;
+  const bool aligned = (d.L & 31) == 0;
+  d.ntiles = aligned ? (d.R + kThreads - 1) / kThreads : (d.R + kScanRows - 1) / kScanRows;
   d.S3 = S < 8 ? S : 8;
   d.logS3 = logS < 3 ? logS : 3;
   f.k2_smem = (size_t)(2 * k2_stage_words((int)TR, d.W)) * 4;
@@ -1850,12 +2425,16 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.bits_stride = (int64_t)align_up((size_t)(f.nwords + 8), 64);
   f.nchunks = (f.V + 1023) / 1024;
   f.sums_stride = (int64_t)align_up((size_t)(f.nchunks + 2), 32);
+  // Unit list: room for one word in eight of the volume to have output, plus
+  // the sentinel; a surface with more units is emitted row-wise instead.
+  f.unit_cap = aligned ? f.nwords / 8 + 1024 : 0;
+  if (f.nwords > 0xffffffffLL) return false;  // unit and row indices are uint32
   size_t o = 0;
   f.off_info = o;   o = align_up(o + (size_t)niso * 16 * 8, 256);
   f.off_flags = o;  o = align_up(o + (size_t)niso * d.ntiles * 4, 256);
   f.reset_bytes = o;
-  f.off_agg = o;    o = align_up(o + (size_t)niso * d.ntiles * 4 * 8, 256);
-  f.off_incl = o;   o = align_up(o + (size_t)niso * d.ntiles * 4 * 8, 256);
+  f.off_agg = o;    o = align_up(o + (size_t)niso * d.ntiles * 5 * 8, 256);
+  f.off_incl = o;   o = align_up(o + (size_t)niso * d.ntiles * 5 * 8, 256);
   f.off_tot = o;    o = align_up(o + (size_t)niso * 4 * 8, 256);
   f.off_base = o;   o = align_up(o + (size_t)niso * 8 * 8, 256);
   f.off_cnt = o;    o = align_up(o + (size_t)niso * d.R * 4 * 4, 256);
@@ -1864,6 +2443,10 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.off_work = o;   o = align_up(o + (size_t)niso * d.R * 4, 256);
   f.off_bits = o;   o = align_up(o + (size_t)niso * f.bits_stride * 4, 256);
   f.off_sums = o;   o = align_up(o + (size_t)niso * f.sums_stride * 8, 256);
+  f.off_ufirst = o; o = align_up(o + (aligned ? (size_t)niso * d.R * 4 : 0), 256);
+  f.off_ucnt = o;   o = align_up(o + (aligned ? (size_t)niso * d.R * 4 : 0), 256);
+  f.off_uslot = o;  o = align_up(o + (aligned ? (size_t)niso * d.R * kUnitSlots * 8 : 0), 256);
+  f.off_units = o;  o = align_up(o + (size_t)niso * f.unit_cap * sizeof(FeUnit), 256);
   f.total = o;
   *out = f;
   return true;
@@ -1882,8 +2465,12 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
     w.tot = reinterpret_cast<long long*>(b + f.off_tot) + (size_t)q * 4;
     w.work = reinterpret_cast<uint32_t*>(b + f.off_work) + (size_t)q * f.d.R;
     w.flags = reinterpret_cast<uint32_t*>(b + f.off_flags) + (size_t)q * f.d.ntiles;
-    w.agg = reinterpret_cast<long long*>(b + f.off_agg) + (size_t)q * f.d.ntiles * 4;
-    w.incl = reinterpret_cast<long long*>(b + f.off_incl) + (size_t)q * f.d.ntiles * 4;
+    w.agg = reinterpret_cast<long long*>(b + f.off_agg) + (size_t)q * f.d.ntiles * 5;
+    w.incl = reinterpret_cast<long long*>(b + f.off_incl) + (size_t)q * f.d.ntiles * 5;
+    w.ufirst = reinterpret_cast<uint32_t*>(b + f.off_ufirst) + (size_t)q * f.d.R;
+    w.units = reinterpret_cast<FeUnit*>(b + f.off_units) + (size_t)q * f.unit_cap;
+    w.ucnt = reinterpret_cast<uint32_t*>(b + f.off_ucnt) + (size_t)q * f.d.R;
+    w.uslot = reinterpret_cast<uint2*>(b + f.off_uslot) + (size_t)q * f.d.R * kUnitSlots;
     w.info = reinterpret_cast<long long*>(b + f.off_info) + (size_t)q * 16;
   }
   return a;
@@ -2138,16 +2725,21 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   TK_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + f.off_info, 0, f.reset_bytes - f.off_info, st));
   const int64_t skip = g_skip_tile.exchange(-1);
-  if ((f.d.L & 31) == 0) {
-    k_fe_count_sparse<<<dim3((unsigned)((f.d.R + kThreads - 1) / kThreads), (unsigned)niso),
-                        kThreads, 0, st>>>(f.d, v, mask);
-  } else {
-    if (f.k2_smem > 48 * 1024)
-      TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)f.k2_smem));
-    k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso), kThreads, f.k2_smem, st>>>(
-        f.d, v, mask, f.nwords);
+  if ((f.d.L & 31) == 0) {  // no waits between blocks here: the skip hook does not apply
+    const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
+    k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
+    TK_LAUNCHED();
+    k_fe_scan_tiles<<<dim3(1, (unsigned)niso), 1024, 0, st>>>(f.d, v, f.unit_cap);
+    TK_LAUNCHED();
+    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, mask, f.unit_cap);
+    TK_LAUNCHED();
+    return TKMC_OK;
   }
+  if (f.k2_smem > 48 * 1024)
+    TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)f.k2_smem));
+  k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso), kThreads, f.k2_smem, st>>>(
+      f.d, v, mask, f.nwords);
   TK_LAUNCHED();
   k_fe_scan_rows<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
       f.d, v, g_wait_ns.load(), skip);
@@ -2257,8 +2849,14 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
     const size_t smem = sizeof(EmitSmem);
     TK_CUDA(cudaFuncSetAttribute(k_fe_emit_words, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem));
+    if (f.unit_cap > 0) {
+      k_fe_emit_units<<<dim3((unsigned)(sm_count() * 8), (unsigned)niso), kThreads, 0, st>>>(
+          f.d, v, A, f.unit_cap);
+      TK_LAUNCHED();
+    }
     const int g = grid_for(f.d.n_own_rows, kThreads, 3);
-    k_fe_emit_words<<<dim3((unsigned)g, (unsigned)niso), kThreads, smem, st>>>(f.d, v, A);
+    k_fe_emit_words<<<dim3((unsigned)g, (unsigned)niso), kThreads, smem, st>>>(f.d, v, A,
+                                                                              f.unit_cap);
   } else {
     const int G = 32 >> f.d.logS3;
     const int g = grid_for(f.d.n_own_rows, (kThreads / 32) * G, 8);

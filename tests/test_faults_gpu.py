@@ -62,3 +62,4 @@ def test_scan_wait_expires_with_status(tack, short_wait):
                            ctypes.byref(tot), stream())
     assert rc == 0 and tot.value == n
     assert torch.equal(out.cpu(), torch.arange(n, dtype=torch.int32))
+

@@ -223,3 +223,31 @@ def test_long_rows_match_oracle(tack, oracle, shape):
             assert got["total_points"] == 0 or got["total_tris"] == 0
         else:
             assert_same_surface(got, ref)
+
+
+@pytest.mark.parametrize("shape,density", [((255, 127, 30), "noise"), ((127, 63, 40), "smooth"),
+                                           ((2047, 6, 5), "smooth")])
+def test_word_aligned_rows_units_and_fallback(tack, oracle, shape, density):
+    """Rows of a multiple of 32 nodes take the unit-list path.  White noise
+    makes nearly every word active, more units than the workspace's unit list
+    holds: the row-wise emit kernel must take over with the same result."""
+    nx, ny, nz = shape
+    assert (nx + 1) % 32 == 0
+    rng = np.random.default_rng(nx + ny)
+    n = (nx + 1) * (ny + 1) * (nz + 1)
+    if density == "noise":
+        v = rng.standard_normal(n).astype(np.float32)
+    else:
+        z, y, x = np.meshgrid(np.arange(nz + 1), np.arange(ny + 1), np.arange(nx + 1),
+                              indexing="ij")
+        v = (np.sin(x * 0.05) + np.cos(y * 0.11) * np.sin(z * 0.07)
+             + 0.05 * rng.standard_normal(x.shape)).astype(np.float32).reshape(-1)
+    g = (nx, ny, nz, -3.0, 0.5, 1.0, 0.1, 0.2, 0.3)
+    for iso in (0.0, 0.4):
+        got = capi_fe(v, g, [iso], want_rows=True)
+        info = oracle.count_block(v, oracle.Grid(*g), iso)
+        xo, yo, zo, to = reference_offsets_from_rows(got["rows"][0], got["counts"][0], g)
+        np.testing.assert_array_equal(xo, info["xo"])
+        np.testing.assert_array_equal(to, info["tri_offsets"])
+        ref = oracle.flying_edges(v, oracle.Grid(*g), iso)
+        assert_same_surface(got, ref)
