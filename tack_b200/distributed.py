@@ -130,6 +130,9 @@ class SlabEngine:
         world = plan.world
         self.gathered = torch.zeros(world * len(self.isos) * 4, dtype=torch.int64,
                                     device=self.dev)
+        # Device-side plan: this rank's totals and its output bases.
+        self.counts_dev = torch.zeros(len(self.isos) * 4, dtype=torch.int64, device=self.dev)
+        self.bases_dev = torch.zeros(len(self.isos) * 7, dtype=torch.int64, device=self.dev)
 
     def count(self, local_values):
         g, p, lib = self.grid, self.plan, self.lib
@@ -159,6 +162,55 @@ class SlabEngine:
                 _i64(bases["out_base"]), _i64(bases["tri_out"]), pts.data_ptr(), own_p,
                 conn.data_ptr(), own_t, current_stream(self.dev)), "tkmc_fe_emit")
         return pts[:own_p * 3], conn[:own_t * 3]
+
+    def run_device(self, local_values, points, conn, counts_host=None, marks=None):
+        """count -> totals all-gather (NCCL, device buffers) -> plan -> emit,
+        with nothing read on the host in between.  points / conn are flat
+        f32 / int32 CUDA tensors whose sizes are the capacities; writes past
+        them are skipped and reported by check().  When counts_host (pinned
+        int64, niso*4) is given, this rank's totals are copied there
+        asynchronously.  Every rank takes the same collective each call.
+        marks: optional 5 CUDA events, recorded before the classify, scan,
+        plan and emit phases and after the emit (phase timing)."""
+        import torch.distributed as dist
+        g, p, lib = self.grid, self.plan, self.lib
+        niso = len(self.isos)
+        st = current_stream(self.dev)
+        isos = _f32(self.isos)
+        ghost = 1 if p.ghost else 0
+
+        def mark(i):
+            if marks is not None:
+                marks[i].record(torch.cuda.current_stream(self.dev))
+
+        mark(0)
+        _lib.check(lib.tkmc_fe_classify(local_values.data_ptr(), g.nx, g.ny, p.nz_cells, isos,
+                                        niso, self.ws.data_ptr(), self.nbytes, st),
+                   "tkmc_fe_classify")
+        mark(1)
+        _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, p.nz_cells, ghost, niso, None,
+                                    self.ws.data_ptr(), self.nbytes, st), "tkmc_fe_scan")
+        mark(2)
+        _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, p.nz_cells, niso, self.ws.data_ptr(),
+                                           self.nbytes, self.counts_dev.data_ptr(), st),
+                   "tkmc_fe_copy_counts")
+        src = self.counts_dev
+        if p.world > 1:
+            dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
+            src = self.gathered
+        _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso,
+                                    self.bases_dev.data_ptr(), st), "tkmc_fe_plan")
+        mark(3)
+        _lib.check(lib.tkmc_fe_emit_dev(
+            local_values.data_ptr(), g.nx, g.ny, p.nz_cells, ghost, p.k0,
+            _f32([g.x0, g.y0, g.z0, g.dx, g.dy, g.dz]), isos, niso, None, self.ws.data_ptr(),
+            self.nbytes, self.bases_dev.data_ptr(), points.data_ptr(), points.numel() // 3,
+            conn.data_ptr(), conn.numel() // 3, st), "tkmc_fe_emit_dev")
+        mark(4)
+        if counts_host is not None:
+            _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, p.nz_cells, niso, self.ws.data_ptr(),
+                                               self.nbytes, counts_host.data_ptr(), st),
+                       "tkmc_fe_copy_counts")
 
     def check(self):
         """Synchronise and raise if the device recorded an error."""

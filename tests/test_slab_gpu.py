@@ -98,3 +98,84 @@ def test_two_gpu_torchrun_nccl(tmp_path):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=700)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert out.read_text().strip() == "ok"
+
+
+def test_device_planned_emit_matches_host_planned(tack):
+    """copy_counts -> plan -> emit_dev (bases in device memory) gives the same
+    bytes as the host-planned emit, for every rank of a 3-way split, and a
+    too-small output is reported, cleared and redone."""
+    import ctypes
+    from tack_b200 import _lib
+    from tack_b200.distributed import SlabEngine, SlabPlan, slab_bases
+    from fe_helpers import f32arr, stream
+    lib = _lib.load()
+    nx, ny, nz = 95, 70, 41
+    rng = np.random.default_rng(7)
+    z, y, x = np.meshgrid(np.arange(nz + 1), np.arange(ny + 1), np.arange(nx + 1), indexing="ij")
+    v = (np.sin(x * 0.2) + np.cos(y * 0.15 + z * 0.1) + 0.1 * rng.standard_normal(x.shape))
+    vol = torch.from_numpy(v.astype(np.float32).reshape(-1)).cuda()
+    g = tack.UniformGrid(nx, ny, nz, 0.5, 1.0, -2.0, 0.25, 0.5, 0.75)
+    isos = [0.0, 0.7]
+    world, niso = 3, len(isos)
+    plane = (nx + 1) * (ny + 1)
+    plans = [SlabPlan(nz + 1, world, r) for r in range(world)]
+    engs = [SlabEngine(g, p, isos) for p in plans]
+    slabs = [vol[p.k0 * plane:p.k1 * plane] for p in plans]
+    counts = [e.count(sv) for e, sv in zip(engs, slabs)]
+    allc = np.stack(counts)
+    gathered = torch.zeros(world * niso * 4, dtype=torch.int64, device="cuda")
+    st = stream()
+    for r, e in enumerate(engs):
+        dst = gathered[r * niso * 4:(r + 1) * niso * 4]
+        assert lib.tkmc_fe_copy_counts(nx, ny, plans[r].nz_cells, niso, e.ws.data_ptr(),
+                                       e.nbytes, dst.data_ptr(), st) == 0
+    geom = f32arr([g.x0, g.y0, g.z0, g.dx, g.dy, g.dz])
+    for r, (p, e, sv) in enumerate(zip(plans, engs, slabs)):
+        b = slab_bases(allc, r)
+        want_p, want_c = e.emit(sv, counts[r], b)
+        bases = torch.zeros(niso * 7, dtype=torch.int64, device="cuda")
+        assert lib.tkmc_fe_plan(gathered.data_ptr(), world, r, niso, bases.data_ptr(), st) == 0
+        host_b = np.concatenate([b["id_base"], b["out_base"], b["tri_out"][:, None]], axis=1)
+        np.testing.assert_array_equal(bases.cpu().numpy().reshape(niso, 7), host_b)
+        P, T = int(counts[r][:, :3].sum()), int(counts[r][:, 3].sum())
+        ghost = 1 if p.ghost else 0
+        # Too small first: the emit skips what does not fit and reports it.
+        small_p = torch.empty(3 * max(P // 2, 1), dtype=torch.float32, device="cuda")
+        small_c = torch.empty(3 * max(T // 2, 1), dtype=torch.int32, device="cuda")
+        args = (sv.data_ptr(), nx, ny, p.nz_cells, ghost, p.k0, geom, f32arr(isos), niso, None,
+                e.ws.data_ptr(), e.nbytes, bases.data_ptr())
+        assert lib.tkmc_fe_emit_dev(*args, small_p.data_ptr(), small_p.numel() // 3,
+                                    small_c.data_ptr(), small_c.numel() // 3, st) == 0
+        assert lib.tkmc_fe_check(nx, ny, p.nz_cells, niso, e.ws.data_ptr(), e.nbytes,
+                                 st) == _lib.TKMC_ERR_CAPACITY
+        assert lib.tkmc_fe_clear_capacity_error(nx, ny, p.nz_cells, niso, e.ws.data_ptr(),
+                                                e.nbytes, st) == 0
+        pts = torch.empty(3 * P, dtype=torch.float32, device="cuda")
+        cn = torch.empty(3 * T, dtype=torch.int32, device="cuda")
+        assert lib.tkmc_fe_emit_dev(*args, pts.data_ptr(), P, cn.data_ptr(), T, st) == 0
+        assert lib.tkmc_fe_check(nx, ny, p.nz_cells, niso, e.ws.data_ptr(), e.nbytes, st) == 0
+        assert torch.equal(pts.view(torch.int32), want_p.view(torch.int32))
+        assert torch.equal(cn, want_c)
+    del ctypes
+
+
+def test_run_device_single_volume(tack):
+    """SlabEngine.run_device on one GPU (world 1) equals the host-planned run."""
+    from tack_b200 import workloads
+    from tack_b200.distributed import SlabEngine, SlabPlan
+    shape = (128, 96, 80)
+    vol = workloads.generate("blobs", shape)
+    g = tack.UniformGrid(shape[0] - 1, shape[1] - 1, shape[2] - 1, 0, 0, 0, 1, 1, 1)
+    eng = SlabEngine(g, SlabPlan(shape[2], 1, 0), [0.5, 0.9])
+    ref = eng.run(vol)
+    P = int(ref["counts"][:, :3].sum())
+    T = int(ref["counts"][:, 3].sum())
+    pts = torch.empty(3 * P, dtype=torch.float32, device="cuda")
+    cn = torch.empty(3 * T, dtype=torch.int32, device="cuda")
+    counts_host = torch.zeros(8, dtype=torch.int64, pin_memory=True)
+    for _ in range(2):
+        eng.run_device(vol, pts, cn, counts_host)
+    eng.check()
+    np.testing.assert_array_equal(counts_host.numpy().reshape(2, 4), ref["counts"])
+    assert torch.equal(pts.view(torch.int32), ref["points_field"].tensor.view(torch.int32))
+    assert torch.equal(cn, ref["conn_field"].tensor)
