@@ -2562,6 +2562,22 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
   return a;
 }
 
+// Raise a kernel's dynamic shared memory limit once per device (and size),
+// so that launch sequences need no attribute calls (they may be captured
+// into CUDA graphs).
+template <typename F>
+int ensure_smem(F* kernel, size_t bytes, std::atomic<size_t>* per_device) {
+  int dev = 0;
+  TK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_err(TKMC_ERR_CUDA, "device index %d out of range", dev);
+  if (per_device[dev].load() >= bytes) return TKMC_OK;
+  TK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  per_device[dev].store(bytes);
+  return TKMC_OK;
+}
+std::atomic<size_t> g_smem_count[64];
+std::atomic<size_t> g_smem_emit_words[64];
+
 int check_ws(void* ws, size_t have, size_t need) {
   if (need && !ws) return set_err(TKMC_ERR_INVALID_ARG, "workspace is NULL");
   if (have < need)
@@ -2822,8 +2838,7 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
     return TKMC_OK;
   }
   if (f.k2_smem > 48 * 1024)
-    TK_CUDA(cudaFuncSetAttribute(k_fe_count, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)f.k2_smem));
+    if ((rc = ensure_smem(k_fe_count, f.k2_smem, g_smem_count))) return rc;
   k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso), kThreads, f.k2_smem, st>>>(
       f.d, v, mask, f.nwords);
   TK_LAUNCHED();
@@ -2936,8 +2951,7 @@ static int fe_emit_impl(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (f.d.AW <= kMaxAW) {
     const size_t smem = sizeof(EmitSmem);
-    TK_CUDA(cudaFuncSetAttribute(k_fe_emit_words, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
+    if ((rc = ensure_smem(k_fe_emit_words, smem, g_smem_emit_words))) return rc;
     if (f.unit_cap > 0) {
       k_fe_emit_units<<<dim3((unsigned)(sm_count() * 8), (unsigned)niso), kThreads, 0, st>>>(
           f.d, v, A, f.unit_cap);

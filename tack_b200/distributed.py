@@ -212,6 +212,22 @@ class SlabEngine:
                                                self.nbytes, counts_host.data_ptr(), st),
                        "tkmc_fe_copy_counts")
 
+    def capture(self, local_values, points, conn, counts_host=None):
+        """Record run_device into a CUDA graph; each replay() is one isosurface
+        of local_values (same buffers) with a single launch from the host.
+        Single GPU only (world 1: the graph holds no collective)."""
+        if self.plan.world != 1:
+            raise ValueError("graph capture is for world 1 (no collective inside)")
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(side):
+            self.run_device(local_values, points, conn, counts_host)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self.run_device(local_values, points, conn, counts_host)
+        return graph
+
     def check(self):
         """Synchronise and raise if the device recorded an error."""
         g, p = self.grid, self.plan

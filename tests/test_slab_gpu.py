@@ -179,3 +179,32 @@ def test_run_device_single_volume(tack):
     np.testing.assert_array_equal(counts_host.numpy().reshape(2, 4), ref["counts"])
     assert torch.equal(pts.view(torch.int32), ref["points_field"].tensor.view(torch.int32))
     assert torch.equal(cn, ref["conn_field"].tensor)
+
+
+def test_graph_replay_single_volume(tack):
+    """The device-planned step captured in a CUDA graph: each replay rewrites
+    the same bytes as the host-planned run."""
+    from tack_b200 import workloads
+    from tack_b200.distributed import SlabEngine, SlabPlan
+    shape = (160, 96, 64)
+    vol = workloads.generate("gyroid", shape)
+    g = tack.UniformGrid(shape[0] - 1, shape[1] - 1, shape[2] - 1, 0, 0, 0, 1, 1, 1)
+    eng = SlabEngine(g, SlabPlan(shape[2], 1, 0), [0.0])
+    ref = eng.run(vol)
+    P = int(ref["counts"][:, :3].sum())
+    T = int(ref["counts"][:, 3].sum())
+    pts = torch.empty(3 * P, dtype=torch.float32, device="cuda")
+    cn = torch.empty(3 * T, dtype=torch.int32, device="cuda")
+    counts_host = torch.zeros(4, dtype=torch.int64, pin_memory=True)
+    graph = eng.capture(vol, pts, cn, counts_host)
+    for _ in range(3):
+        pts.zero_()
+        cn.zero_()
+        counts_host.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        eng.check()
+        np.testing.assert_array_equal(counts_host.numpy().reshape(1, 4), ref["counts"])
+        assert torch.equal(pts.view(torch.int32), ref["points_field"].tensor.view(torch.int32))
+        assert torch.equal(cn, ref["conn_field"].tensor)
+    del graph
