@@ -188,12 +188,15 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
                         int64_t* dst, void* stream);
 
 /* Device-side planning: from DEVICE all_counts_dev[world][niso][4] (the
- * totals of every z-slab rank; for one volume world = 1 and the workspace's
- * own totals) write bases_dev[niso*7] for rank `rank`: point ids in the
- * single-volume layout, rows in the rank-local output.  The sums of
- * tack_b200.distributed.slab_bases.  Asynchronous. */
+ * totals of every z-slab part, in z order; for one volume world = 1 and the
+ * workspace's own totals) write bases_dev[niso*7] for part `rank`: point ids
+ * in the single-volume layout, and output rows either in a part-local output
+ * (shared_output = 0: the part's x, y, z points then its triangles, per
+ * isovalue; the sums of tack_b200.distributed.slab_bases) or in one shared
+ * single-volume output (shared_output != 0: rows = ids, triangle rows
+ * global).  Asynchronous. */
 int tkmc_fe_plan(const int64_t* all_counts_dev, int world, int rank, int niso,
-                 int64_t* bases_dev, void* stream);
+                 int shared_output, int64_t* bases_dev, void* stream);
 
 /* Forget TKMC_ERR_CAPACITY recorded by an emit into too-small buffers, so
  * that the emit can be repeated into larger ones (device timeouts stay

@@ -2264,9 +2264,9 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
 // output (isovalue-major; x, y, z sections of this rank).  The same sums as
 // the host's slab_bases.
 __global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, int niso,
-                          long long* __restrict__ bases) {
+                          int shared_output, long long* __restrict__ bases) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  long long Pq = 0, lp = 0, lt = 0;
+  long long Pq = 0, Tq = 0, lp = 0, lt = 0;
   for (int q = 0; q < niso; ++q) {
     long long tot[4] = {0, 0, 0, 0}, before[4] = {0, 0, 0, 0}, own[4];
     for (int r = 0; r < world; ++r)
@@ -2280,11 +2280,19 @@ __global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, 
     b[0] = Pq + before[0];
     b[1] = Pq + tot[0] + before[1];
     b[2] = Pq + tot[0] + tot[1] + before[2];
-    b[3] = lp;
-    b[4] = lp + own[0];
-    b[5] = lp + own[0] + own[1];
-    b[6] = lt;
+    if (shared_output) {  // every part writes into one single-volume output
+      b[3] = b[0];
+      b[4] = b[1];
+      b[5] = b[2];
+      b[6] = Tq + before[3];
+    } else {
+      b[3] = lp;
+      b[4] = lp + own[0];
+      b[5] = lp + own[0] + own[1];
+      b[6] = lt;
+    }
     Pq += tot[0] + tot[1] + tot[2];
+    Tq += tot[3];
     lp += own[0] + own[1] + own[2];
     lt += own[3];
   }
@@ -3005,12 +3013,12 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso, const void
 }
 
 int tkmc_fe_plan(const int64_t* all_counts_dev, int world, int rank, int niso,
-                 int64_t* bases_dev, void* stream) {
+                 int shared_output, int64_t* bases_dev, void* stream) {
   if (!all_counts_dev || !bases_dev) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_plan: NULL");
   if (world < 1 || rank < 0 || rank >= world || niso < 1 || niso > TKMC_MAX_ISO)
     return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_plan: bad world/rank/niso");
   k_fe_plan<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const long long*>(all_counts_dev), world, rank, niso,
+      reinterpret_cast<const long long*>(all_counts_dev), world, rank, niso, shared_output,
       reinterpret_cast<long long*>(bases_dev));
   TK_LAUNCHED();
   return TKMC_OK;

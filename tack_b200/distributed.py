@@ -198,7 +198,7 @@ class SlabEngine:
         if p.world > 1:
             dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
             src = self.gathered
-        _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso,
+        _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso, 0,
                                     self.bases_dev.data_ptr(), st), "tkmc_fe_plan")
         mark(3)
         _lib.check(lib.tkmc_fe_emit_dev(

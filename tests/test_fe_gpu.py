@@ -251,3 +251,24 @@ def test_word_aligned_rows_units_and_fallback(tack, oracle, shape, density):
         np.testing.assert_array_equal(to, info["tri_offsets"])
         ref = oracle.flying_edges(v, oracle.Grid(*g), iso)
         assert_same_surface(got, ref)
+
+
+
+@pytest.mark.parametrize("shape", [(2, 2, 2), (30, 20, 9), (159, 160, 161), (255, 255, 255),
+                                   (1023, 3, 2)])
+def test_volume_sizes_match_oracle(tack, oracle, shape):
+    """Volumes of one to many 1024-node chunks per warp of the threshold
+    pass, with ragged tails shorter than 16 bytes."""
+    nx, ny, nz = shape
+    n = (nx + 1) * (ny + 1) * (nz + 1)
+    rng = np.random.default_rng(n % 1000)
+    i = np.arange(n, dtype=np.int64)
+    v = (np.sin(i % (nx + 1) * 0.07) + np.cos(i // ((nx + 1) * (ny + 1)) * 0.05)
+         + 0.3 * rng.standard_normal(n)).astype(np.float32)
+    g = (nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+    ref = oracle.flying_edges(v, oracle.Grid(*g), 0.4)
+    got = capi_fe(v, g, [0.4])
+    if ref is None:
+        assert got["total_points"] == 0 or got["total_tris"] == 0
+    else:
+        assert_same_surface(got, ref)

@@ -134,7 +134,7 @@ def test_device_planned_emit_matches_host_planned(tack):
         b = slab_bases(allc, r)
         want_p, want_c = e.emit(sv, counts[r], b)
         bases = torch.zeros(niso * 7, dtype=torch.int64, device="cuda")
-        assert lib.tkmc_fe_plan(gathered.data_ptr(), world, r, niso, bases.data_ptr(), st) == 0
+        assert lib.tkmc_fe_plan(gathered.data_ptr(), world, r, niso, 0, bases.data_ptr(), st) == 0
         host_b = np.concatenate([b["id_base"], b["out_base"], b["tri_out"][:, None]], axis=1)
         np.testing.assert_array_equal(bases.cpu().numpy().reshape(niso, 7), host_b)
         P, T = int(counts[r][:, :3].sum()), int(counts[r][:, 3].sum())
@@ -208,3 +208,44 @@ def test_graph_replay_single_volume(tack):
         assert torch.equal(pts.view(torch.int32), ref["points_field"].tensor.view(torch.int32))
         assert torch.equal(cn, ref["conn_field"].tensor)
     del graph
+
+
+def test_shared_output_plan_single_gpu_parts(tack, oracle):
+    """Several z-parts on one GPU planned with shared_output=1 write one
+    output in the single-volume layout: equal to the oracle's surface."""
+    from tack_b200 import _lib
+    from tack_b200.distributed import SlabEngine, SlabPlan
+    from fe_helpers import f32arr, stream
+    lib = _lib.load()
+    nx, ny, nz = 127, 40, 50
+    rng = np.random.default_rng(3)
+    z, y, x = np.meshgrid(np.arange(nz + 1), np.arange(ny + 1), np.arange(nx + 1), indexing="ij")
+    v = (np.cos(x * 0.1) * np.sin(y * 0.2) + np.sin(z * 0.15)
+         + 0.05 * rng.standard_normal(x.shape)).astype(np.float32).reshape(-1)
+    vol = torch.from_numpy(v).cuda()
+    g = tack.UniformGrid(nx, ny, nz, 1.0, 2.0, 3.0, 0.5, 0.5, 0.5)
+    isos = [0.1, -0.4]
+    parts, niso = 4, len(isos)
+    plane = (nx + 1) * (ny + 1)
+    plans = [SlabPlan(nz + 1, parts, r) for r in range(parts)]
+    engs = [SlabEngine(g, p, isos) for p in plans]
+    slabs = [vol[p.k0 * plane:p.k1 * plane] for p in plans]
+    counts = np.stack([e.count(sv) for e, sv in zip(engs, slabs)])
+    P, T = int(counts[:, :, :3].sum()), int(counts[:, :, 3].sum())
+    dev_counts = torch.from_numpy(counts.reshape(-1).copy()).cuda()
+    pts = torch.zeros(3 * P, dtype=torch.float32, device="cuda")
+    cn = torch.zeros(3 * T, dtype=torch.int32, device="cuda")
+    geom = f32arr([g.x0, g.y0, g.z0, g.dx, g.dy, g.dz])
+    st = stream()
+    for r, (p, e, sv) in enumerate(zip(plans, engs, slabs)):
+        bases = torch.zeros(niso * 7, dtype=torch.int64, device="cuda")
+        assert lib.tkmc_fe_plan(dev_counts.data_ptr(), parts, r, niso, 1, bases.data_ptr(), st) == 0
+        assert lib.tkmc_fe_emit_dev(sv.data_ptr(), nx, ny, p.nz_cells, 1 if p.ghost else 0, p.k0,
+                                    geom, f32arr(isos), niso, None, e.ws.data_ptr(), e.nbytes,
+                                    bases.data_ptr(), pts.data_ptr(), P, cn.data_ptr(), T,
+                                    st) == 0
+        assert lib.tkmc_fe_check(nx, ny, p.nz_cells, niso, e.ws.data_ptr(), e.nbytes, st) == 0
+    ref = oracle.flying_edges_isovalues(v, oracle.Grid(nx, ny, nz, g.x0, g.y0, g.z0, g.dx, g.dy,
+                                                       g.dz), isos)
+    np.testing.assert_array_equal(cn.cpu().numpy().reshape(-1, 3), ref["conn"])
+    assert_points_identical(pts.cpu().numpy().reshape(-1, 3), ref["points"])
