@@ -226,8 +226,10 @@ int tkmc_fe_read_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
                         void* workspace, size_t workspace_bytes,
                         int64_t* counts, void* stream);
 
-/* Copy to HOST the per-node-row exclusive offsets that the last
- * tkmc_fe_count / tkmc_fe_scan left in the workspace for isovalue `iso`:
+/* Copy to HOST the per-node-row exclusive offsets of the last
+ * tkmc_fe_count / tkmc_fe_scan for isovalue `iso` (for rows of a multiple of
+ * 32 nodes, whose count pass keeps offsets per word, the row table is first
+ * filled in the workspace from the per-row counts):
  * out[4*r + s], s = 0..3: x, y, z point offsets (each relative to its own
  * section) and triangle offset of node row r = k*(ny+1) + j (the triangle
  * offset of the cell row (j, k) when j < ny and k < nz).  (ny+1)*(nz+1)

@@ -416,6 +416,7 @@ struct FeIsoWs {
   uint2* uslot;         // [R][kUnitSlots] {word, packed counts} of a row's first units
   FeUnit* units;        // units in (row, word) order, then a sentinel with the totals
   uint32_t* flags;      // [ntiles] (scan tiles of kScanRows rows)
+  long long* super;     // [ntiles / kSuperTiles + 1][5] super-tile totals (word-aligned rows)
   long long* agg;       // [ntiles][4]
   long long* incl;      // [ntiles][4]
   long long* info;      // [16]: 0-3 own totals, 4-7 all-row totals, 8 active rows,
@@ -849,6 +850,7 @@ __device__ __forceinline__ uint32_t count_word(const WordQuad& x, const RowQuad&
 }
 
 constexpr int kUnitSlots = 8;  // units per row remembered between the count and offsets passes
+constexpr int kSuperTiles = 64;  // count tiles per super-tile total
 
 __device__ __forceinline__ void put_unit(FeUnit* units, int64_t cap, int64_t ui, uint32_t r,
                                          uint32_t w, const long long (&o)[4]) {
@@ -982,99 +984,24 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
 #pragma unroll
     for (int w2 = 0; w2 < kThreads / 32; ++w2) x += s_red[tid][w2];
     Wk.agg[blockIdx.x * 5 + tid] = x;
+    atomicAdd(reinterpret_cast<unsigned long long*>(Wk.super + (blockIdx.x / kSuperTiles) * 5 + tid),
+              (unsigned long long)x);
   }
 }
 
-// K2b (word-aligned rows): exclusive scan of the tiles' totals by one block
-// per isovalue (the tiles are few: one per 256 rows) into incl[tile], the
-// all-row totals, and the sentinel unit after the last one.  Each thread
-// takes kTilesPerThread consecutive tiles per round.
-constexpr int kScanTilesThreads = 1024, kTilesPerThread = 4;
-
-__global__ void __launch_bounds__(kScanTilesThreads)
-k_fe_scan_tiles(FeDims d, FeWsAll ws, int64_t unit_cap) {
-  __shared__ long long s_w[5][32];
-  __shared__ long long s_carry[5];
-  const FeIsoWs& Wk = ws.iso[blockIdx.y];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid < 5) s_carry[tid] = 0;
-  __syncthreads();
-  constexpr int64_t kRound = (int64_t)kScanTilesThreads * kTilesPerThread;
-  for (int64_t t0 = 0; t0 < d.ntiles; t0 += kRound) {
-    const int64_t tb = t0 + (int64_t)tid * kTilesPerThread;
-    long long v[kTilesPerThread][5];
-    long long mine[5] = {0, 0, 0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < kTilesPerThread; ++i)
-#pragma unroll
-      for (int k = 0; k < 5; ++k) {
-        v[i][k] = tb + i < d.ntiles ? __ldcg(Wk.agg + (tb + i) * 5 + k) : 0;
-        mine[k] += v[i][k];
-      }
-    long long inc[5];
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      long long x = mine[k];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const long long y = __shfl_up_sync(0xffffffffu, x, o);
-        if (lane >= o) x += y;
-      }
-      inc[k] = x;
-      if (lane == 31) s_w[k][warp] = x;
-    }
-    __syncthreads();
-    if (warp == 0) {  // scan the 32 warp totals in place
-#pragma unroll
-      for (int k = 0; k < 5; ++k) {
-        long long x = s_w[k][lane];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const long long y = __shfl_up_sync(0xffffffffu, x, o);
-          if (lane >= o) x += y;
-        }
-        s_w[k][lane] = x;  // inclusive over warps
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-      long long run = s_carry[k] + (warp ? s_w[k][warp - 1] : 0) + inc[k] - mine[k];
-#pragma unroll
-      for (int i = 0; i < kTilesPerThread; ++i) {
-        if (tb + i < d.ntiles) Wk.incl[(tb + i) * 5 + k] = run;
-        run += v[i][k];
-      }
-    }
-    __syncthreads();
-    if (tid < 5) s_carry[tid] += s_w[tid][31];
-    __syncthreads();
-  }
-  if (tid == 0) {
-    long long all[5];
-#pragma unroll
-    for (int k = 0; k < 5; ++k) all[k] = s_carry[k];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) Wk.info[4 + k] = all[k];
-    Wk.info[11] = all[4];
-    if (d.n_own_rows == d.R) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) Wk.info[k] = Wk.tot[k] = all[k];
-      Wk.info[12] = all[4];
-    }
-    // Sentinel after the last unit: the totals, for lookups past the end.
-    const long long o[4] = {all[0], all[1], all[2], all[3]};
-    put_unit(Wk.units, unit_cap, all[4], (uint32_t)d.R, 0u, o);
-  }
-}
-
-// K2c (word-aligned rows): row offsets, first unit of each row, the units,
-// own totals and the worklist of active own rows.  One thread per row; the
-// tile's prefix comes from the tile scan.
+// K2b (word-aligned rows): the first unit of each row, the units, the
+// totals, and -- only when the unit list overflowed, or when asked
+// (rows_only) -- the row offsets and the worklist of active own rows that the
+// row-wise emit kernel uses.  One thread per row, the same tiles as K2a.
+// The tile's prefix is the sum of the super-tile totals before its super-tile
+// and of the tile totals before it within its super-tile; the grand totals
+// are the sum of all super-tile totals.  No block waits for another.
 __global__ void __launch_bounds__(kThreads)
-k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t unit_cap) {
+k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t unit_cap,
+                   int rows_only) {
   __shared__ int s_ntri[256];
   __shared__ long long s_w[5][kThreads / 32];
+  __shared__ long long s_pre[5], s_all[5];
   __shared__ unsigned s_wbase[kThreads / 32];
   const FeIsoWs& Wk = ws.iso[blockIdx.y];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1082,6 +1009,26 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64
   const int64_t tile = blockIdx.x;
   const int64_t r = tile * kThreads + tid;
   const bool valid = r < d.R;
+  if (warp < 5) {  // warp k sums value k of the tile's prefix and of the grand total
+    const int k = warp;
+    const int64_t nsup = (d.ntiles + kSuperTiles - 1) / kSuperTiles, sup = tile / kSuperTiles;
+    long long pre = 0, all = 0;
+    for (int64_t i = lane; i < nsup; i += 32) {
+      const long long x = (long long)__ldcg(Wk.super + i * 5 + k);
+      all += x;
+      if (i < sup) pre += x;
+    }
+    for (int64_t i = sup * kSuperTiles + lane; i < tile; i += 32) pre += __ldcg(Wk.agg + i * 5 + k);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      pre += __shfl_xor_sync(0xffffffffu, pre, o);
+      all += __shfl_xor_sync(0xffffffffu, all, o);
+    }
+    if (lane == 0) {
+      s_pre[k] = pre;
+      s_all[k] = all;
+    }
+  }
   int4 c = make_int4(0, 0, 0, 0);
   unsigned nU = 0;
   if (valid) {
@@ -1109,12 +1056,19 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64
 #pragma unroll
     for (int w2 = 0; w2 < kThreads / 32; ++w2)
       if (w2 < warp) before += s_w[t][w2];
-    ex[t] = __ldcg(Wk.incl + tile * 5 + t) + before + inc[t] - own[t];
+    ex[t] = s_pre[t] + before + inc[t] - own[t];
   }
+  // The row-wise emit kernel runs instead when the units do not fit.
+  const bool overflow = s_all[4] + 1 > unit_cap;
+  const bool rows = overflow || rows_only;
   if (valid) {
-    longlong2* dst = reinterpret_cast<longlong2*>(Wk.rowoff + r * 4);
-    dst[0] = make_longlong2(ex[0], ex[1]);
-    dst[1] = make_longlong2(ex[2], ex[3]);
+    if (rows) {
+      longlong2* dst = reinterpret_cast<longlong2*>(Wk.rowoff + r * 4);
+      dst[0] = make_longlong2(ex[0], ex[1]);
+      dst[1] = make_longlong2(ex[2], ex[3]);
+    }
+  }
+  if (valid && !rows_only) {
     Wk.ufirst[r] = (uint32_t)ex[4];
     // Own totals: the offsets of the first ghost row.
     if (r == d.n_own_rows) {
@@ -1122,48 +1076,61 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64
       for (int t = 0; t < 4; ++t) Wk.info[t] = Wk.tot[t] = ex[t];
       Wk.info[12] = ex[4];
     }
-    if (nU) {
-      long long o[4] = {ex[0], ex[1], ex[2], ex[3]};
-      int64_t ui = ex[4];
-      if (nU <= kUnitSlots) {
-        // The row's slots are 64 contiguous bytes: load what is used at once.
-        const uint4* sp = reinterpret_cast<const uint4*>(Wk.uslot + r * kUnitSlots);
-        uint4 sv[kUnitSlots / 2];
+    if (r == 0) {
 #pragma unroll
-        for (int i = 0; i < kUnitSlots / 2; ++i)
-          sv[i] = (unsigned)(2 * i) < nU ? __ldcg(sp + i) : make_uint4(0u, 0u, 0u, 0u);
+      for (int t = 0; t < 4; ++t) Wk.info[4 + t] = s_all[t];
+      Wk.info[11] = s_all[4];
+      if (d.n_own_rows == d.R) {
 #pragma unroll
-        for (int i = 0; i < kUnitSlots; ++i) {
-          if ((unsigned)i >= nU) break;
-          const uint32_t sw = (i & 1) ? sv[i >> 1].z : sv[i >> 1].x;
-          const uint32_t sc = (i & 1) ? sv[i >> 1].w : sv[i >> 1].y;
-          put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, sw, o);
-          o[0] += sc & 63u;
-          o[1] += (sc >> 6) & 63u;
-          o[2] += (sc >> 12) & 63u;
-          o[3] += sc >> 18;
-        }
-      } else {  // long active rows: count their active words again
-        const RowQuad q = row_quad(d, r);
-        for (int g = 0; g < d.AW; ++g) {
-          uint32_t act = __ldcg(Wk.wact + r * d.AW + g);
-          while (act) {
-            const int w = 32 * g + __ffs(act) - 1;
-            act &= act - 1u;
-            const uint32_t cw = count_word(load_word_quad(Wk.bits, q, w, d.W), q, w, (int)d.L,
-                                           d, mask, s_ntri);
-            put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, (uint32_t)w, o);
-            o[0] += cw & 63u;
-            o[1] += (cw >> 6) & 63u;
-            o[2] += (cw >> 12) & 63u;
-            o[3] += cw >> 18;
-          }
+        for (int t = 0; t < 4; ++t) Wk.info[t] = Wk.tot[t] = s_all[t];
+        Wk.info[12] = s_all[4];
+      }
+      // Sentinel after the last unit: the totals, for lookups past the end.
+      const long long o[4] = {s_all[0], s_all[1], s_all[2], s_all[3]};
+      put_unit(Wk.units, unit_cap, s_all[4], (uint32_t)d.R, 0u, o);
+    }
+  }
+  if (valid && !rows_only && !overflow && nU) {
+    long long o[4] = {ex[0], ex[1], ex[2], ex[3]};
+    int64_t ui = ex[4];
+    if (nU <= kUnitSlots) {
+      // The row's slots are 64 contiguous bytes: load what is used at once.
+      const uint4* sp = reinterpret_cast<const uint4*>(Wk.uslot + r * kUnitSlots);
+      uint4 sv[kUnitSlots / 2];
+#pragma unroll
+      for (int i = 0; i < kUnitSlots / 2; ++i)
+        sv[i] = (unsigned)(2 * i) < nU ? __ldcg(sp + i) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int i = 0; i < kUnitSlots; ++i) {
+        if ((unsigned)i >= nU) break;
+        const uint32_t sw = (i & 1) ? sv[i >> 1].z : sv[i >> 1].x;
+        const uint32_t sc = (i & 1) ? sv[i >> 1].w : sv[i >> 1].y;
+        put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, sw, o);
+        o[0] += sc & 63u;
+        o[1] += (sc >> 6) & 63u;
+        o[2] += (sc >> 12) & 63u;
+        o[3] += sc >> 18;
+      }
+    } else {  // long active rows: count their active words again
+      const RowQuad q = row_quad(d, r);
+      for (int g = 0; g < d.AW; ++g) {
+        uint32_t act = __ldcg(Wk.wact + r * d.AW + g);
+        while (act) {
+          const int w = 32 * g + __ffs(act) - 1;
+          act &= act - 1u;
+          const uint32_t cw = count_word(load_word_quad(Wk.bits, q, w, d.W), q, w, (int)d.L,
+                                         d, mask, s_ntri);
+          put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, (uint32_t)w, o);
+          o[0] += cw & 63u;
+          o[1] += (cw >> 6) & 63u;
+          o[2] += (cw >> 12) & 63u;
+          o[3] += cw >> 18;
         }
       }
     }
   }
   // Worklist of own rows with any output, for the row-wise emit kernel.
-  const bool act_row = valid && r < d.n_own_rows && nU != 0;
+  const bool act_row = overflow && !rows_only && valid && r < d.n_own_rows && nU != 0;
   const uint32_t bal = __ballot_sync(0xffffffffu, act_row);
   if (lane == 0 && bal)
     s_wbase[warp] = (unsigned)atomicAdd((unsigned long long*)(Wk.info + 8),
@@ -2471,7 +2438,8 @@ struct FeLayout {
   size_t k2_smem;   // dynamic shared memory of the count kernel (rows not word-aligned)
   int64_t V, nwords, bits_stride, nchunks, sums_stride;
   int64_t unit_cap;  // units (incl. the sentinel) the workspace holds; 0: rows not word-aligned
-  size_t off_units, off_ufirst, off_ucnt, off_uslot;
+  size_t off_units, off_ufirst, off_ucnt, off_uslot, off_super;
+  int64_t super_stride;
   size_t off_bits, off_sums, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
   size_t reset_bytes;  // info + flags, zeroed before each scan
@@ -2526,6 +2494,8 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   size_t o = 0;
   f.off_info = o;   o = align_up(o + (size_t)niso * 16 * 8, 256);
   f.off_flags = o;  o = align_up(o + (size_t)niso * d.ntiles * 4, 256);
+  f.super_stride = aligned ? (d.ntiles + kSuperTiles - 1) / kSuperTiles * 5 : 0;
+  f.off_super = o;  o = align_up(o + (size_t)niso * f.super_stride * 8, 256);
   f.reset_bytes = o;
   f.off_agg = o;    o = align_up(o + (size_t)niso * d.ntiles * 5 * 8, 256);
   f.off_incl = o;   o = align_up(o + (size_t)niso * d.ntiles * 5 * 8, 256);
@@ -2559,6 +2529,7 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
     w.tot = reinterpret_cast<long long*>(b + f.off_tot) + (size_t)q * 4;
     w.work = reinterpret_cast<uint32_t*>(b + f.off_work) + (size_t)q * f.d.R;
     w.flags = reinterpret_cast<uint32_t*>(b + f.off_flags) + (size_t)q * f.d.ntiles;
+    w.super = reinterpret_cast<long long*>(b + f.off_super) + (size_t)q * f.super_stride;
     w.agg = reinterpret_cast<long long*>(b + f.off_agg) + (size_t)q * f.d.ntiles * 5;
     w.incl = reinterpret_cast<long long*>(b + f.off_incl) + (size_t)q * f.d.ntiles * 5;
     w.ufirst = reinterpret_cast<uint32_t*>(b + f.off_ufirst) + (size_t)q * f.d.R;
@@ -2839,9 +2810,7 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
     const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
     k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
     TK_LAUNCHED();
-    k_fe_scan_tiles<<<dim3(1, (unsigned)niso), kScanTilesThreads, 0, st>>>(f.d, v, f.unit_cap);
-    TK_LAUNCHED();
-    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, mask, f.unit_cap);
+    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, mask, f.unit_cap, 0);
     TK_LAUNCHED();
     return TKMC_OK;
   }
@@ -2886,6 +2855,11 @@ int tkmc_fe_row_offsets(int64_t nx, int64_t ny, int64_t nz, int niso, int iso,
   if (!out) return set_err(TKMC_ERR_INVALID_ARG, "out is NULL");
   FeWsAll v = fe_views(f, const_cast<void*>(ws), niso);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((f.d.L & 31) == 0) {  // word-aligned rows keep offsets per unit: fill the row table now
+    k_fe_offsets_units<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
+        f.d, v, nullptr, f.unit_cap, 1);
+    TK_LAUNCHED();
+  }
   TK_CUDA(cudaMemcpyAsync(out, v.iso[iso].rowoff, (size_t)f.d.R * 4 * sizeof(long long),
                           cudaMemcpyDeviceToHost, st));
   TK_CUDA(cudaStreamSynchronize(st));
