@@ -103,6 +103,32 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 __constant__ uint64_t c_case_tris[256] = {TKMC_CASE_LIST(TKMC_PACK_CASE)};
 #undef TKMC_PACK_CASE
 
+// The eight edge groups around a cell row of word-granular emission: x(a)
+// y(a) z(a) x(b) x(c) x(d) y(c) z(b), rows a = (j,k), b = (j+1,k),
+// c = (j,k+1), d = (j+1,k+1).
+// Edge e -> (group, +1 node) as nibble g | plus << 3 (edges 0..11).
+constexpr uint64_t kEdgeGroup = 0x0ull | (0x9ull << 4) | (0x3ull << 8) | (0x1ull << 12) |
+                                (0x4ull << 16) | (0xEull << 20) | (0x5ull << 24) |
+                                (0x6ull << 28) | (0x2ull << 32) | (0xAull << 36) |
+                                (0x7ull << 40) | (0xFull << 44);
+
+constexpr uint64_t edge_group(int e) { return (kEdgeGroup >> (4 * e)) & 0xfull; }
+
+// A case's triangle vertices as edge-group nibbles (g | plus << 3), nibble
+// 15 the triangle count: the edge -> group step folded into the table.
+constexpr uint64_t pack_case_groups(const char* s) {
+  uint64_t w = 0;
+  int n = 0;
+  while (s[n]) {
+    w |= edge_group(tkmc::hex_nibble(s[n])) << (4 * n);
+    ++n;
+  }
+  return w | ((uint64_t)(n / 3) << 60);
+}
+#define TKMC_PACK_GROUPS(s) pack_case_groups(s),
+__constant__ uint64_t c_case_groups[256] = {TKMC_CASE_LIST(TKMC_PACK_GROUPS)};
+#undef TKMC_PACK_GROUPS
+
 constexpr int kThreads = 256;
 constexpr int kScanItems = 16;     // generic scan: items per thread
 constexpr int kScanTile = kThreads * kScanItems;
@@ -1315,11 +1341,6 @@ constexpr int kRec = 39;
 constexpr int kRecMasks = 0, kRecAct = 8, kRecBits = 9, kRecOff = 17, kRecTri = 33, kRecJ = 35,
               kRecK = 36, kRecPB = 37, kRecCB = 38;
 
-// Edge e -> (group, +1 node) as nibble g | plus << 3 (edges 0..11).
-constexpr uint64_t kEdgeGroup = 0x0ull | (0x9ull << 4) | (0x3ull << 8) | (0x1ull << 12) |
-                                (0x4ull << 16) | (0xEull << 20) | (0x5ull << 24) |
-                                (0x6ull << 28) | (0x2ull << 32) | (0xAull << 36) |
-                                (0x7ull << 40) | (0xFull << 44);
 
 __device__ __forceinline__ long long rec_i64(const uint32_t* rec, int at) {
   return (long long)(((unsigned long long)rec[at + 1] << 32) | rec[at]);
@@ -2009,7 +2030,8 @@ constexpr int kUAct = 24;  // cut cells of the word
 constexpr int kURow = 25, kUW = 26;  // node row, word
 constexpr int kUPP = 27;   // exclusive prefix of points over the warp's units
 constexpr int kUPC = 28;   // exclusive prefix of cut cells
-constexpr int kUS = 29;
+constexpr int kUCrd = 29;  // f32 bits of y(j), y(j+1), z(k), z(k+1)
+constexpr int kUS = 33;
 
 __device__ __forceinline__ int find_rec(const uint32_t* recs, int field, unsigned e) {
   int lo = 0;
@@ -2019,7 +2041,7 @@ __device__ __forceinline__ int find_rec(const uint32_t* recs, int field, unsigne
   return lo;
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
   __shared__ uint64_t s_case[256];
   __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
@@ -2027,7 +2049,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
   const int isoi = blockIdx.y;
   const FeIsoWs& W = ws.iso[isoi];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  s_case[tid] = c_case_tris[tid];  // kThreads == 256
+  s_case[tid] = c_case_groups[tid];  // kThreads == 256
   __syncthreads();
   const long long n_all = *((volatile long long*)(W.info + 11));
   if (n_all + 1 > unit_cap) return;  // the unit list overflowed: k_fe_emit_words runs instead
@@ -2105,6 +2127,10 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
       rec[kUAct] = act;
       rec[kURow] = (uint32_t)r;
       rec[kUW] = (uint32_t)w;
+      rec[kUCrd + 0] = __float_as_uint(coord(y0, q.j, hy));
+      rec[kUCrd + 1] = __float_as_uint(coord(y0, (int64_t)q.j + 1, hy));
+      rec[kUCrd + 2] = __float_as_uint(coord(z0, (int64_t)q.k + A.k_offset, hz));
+      rec[kUCrd + 3] = __float_as_uint(coord(z0, (int64_t)q.k + 1 + A.k_offset, hz));
       TR[lane] = outT + (long long)(((unsigned long long)u1.w << 32) | u1.z);
       np = __popc(m0) + __popc(m1) + __popc(m2);
       nc = __popc(act);
@@ -2141,10 +2167,8 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
           type = 2; mm = R[kUM + 2]; kk -= cxn + cyn;
         }
         const int bit = nth_set_bit(mm, kk);
-        const int64_t r = R[kURow];
-        const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
         const int64_t n = 32 * (int64_t)R[kUW] + bit;
-        const int64_t node = r * L + n;
+        const int64_t node = (int64_t)R[kURow] * L + n;
         const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
         const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
         const long long row = (long long)R[kUB + type] + kk +
@@ -2154,11 +2178,11 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
         } else {
           const float t = interp_t(iso, s0, s1);
           const float px = coord(x0, n, hx);
-          const float py = coord(y0, j, hy);
-          const float pz = coord(z0, (int64_t)k + A.k_offset, hz);
+          const float py = __uint_as_float(R[kUCrd + 0]);
+          const float pz = __uint_as_float(R[kUCrd + 2]);
           const float px1 = type == 0 ? coord(x0, n + 1, hx) : px;
-          const float py1 = type == 1 ? coord(y0, (int64_t)j + 1, hy) : py;
-          const float pz1 = type == 2 ? coord(z0, (int64_t)k + 1 + A.k_offset, hz) : pz;
+          const float py1 = type == 1 ? __uint_as_float(R[kUCrd + 1]) : py;
+          const float pz1 = type == 2 ? __uint_as_float(R[kUCrd + 3]) : pz;
           float* o = A.points + row * 3;
           o[0] = lerp_ref(px, px1, t);
           o[1] = lerp_ref(py, py1, t);
@@ -2186,7 +2210,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
         }
         if (!masked) {
           pkc = s_case[cell_case(cb, R[kUQ + 0], R[kUQ + 1], R[kUQ + 2], R[kUQ + 3], R[kUQ + 4],
-                                 R[kUQ + 5], R[kUQ + 6], R[kUQ + 7])];
+                                 R[kUQ + 5], R[kUQ + 6], R[kUQ + 7])];  // groups, not edges
           nt = (unsigned)(pkc >> 60);
         }
       }
@@ -2204,8 +2228,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
           const uint32_t below1 = cb == 31 ? 0xffffffffu : ((2u << cb) - 1u);
           int32_t* o = A.conn + tpos * 3;
           for (unsigned t = 0; t < 3 * nt; ++t) {
-            const unsigned ed = (unsigned)(pkc >> (4 * t)) & 0xfu;
-            const unsigned gp = (unsigned)(kEdgeGroup >> (4 * ed)) & 0xfu;
+            const unsigned gp = (unsigned)(pkc >> (4 * t)) & 0xfu;
             const unsigned g = gp & 7u;
             const uint32_t lim = (gp & 8u) ? below1 : below;
             o[t] = (int32_t)(R[kUB + g] + __popc(R[kUM + g] & lim));
