@@ -215,9 +215,9 @@ class SlabEngine:
     def capture(self, local_values, points, conn, counts_host=None):
         """Record run_device into a CUDA graph; each replay() is one isosurface
         of local_values (same buffers) with a single launch from the host.
-        Single GPU only (world 1: the graph holds no collective)."""
-        if self.plan.world != 1:
-            raise ValueError("graph capture is for world 1 (no collective inside)")
+        With several ranks the graph holds the totals all-gather: every rank
+        captures together and replays the same number of times, and the
+        graph is released before the process group is destroyed."""
         side = torch.cuda.Stream(self.dev)
         side.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(side):

@@ -3,7 +3,9 @@
 Each rank generates only its own planes (plus the ghost plane) of a 256^3
 blobs volume, runs SlabEngine (count -> one all-gather of totals -> emit)
 and sends its slices to rank 0, which assembles them and compares the result
-with a single-volume flying_edges call on its own GPU.  Rank 0 writes "ok"
+with a single-volume flying_edges call on its own GPU.  Each rank also
+replays the device-planned step from a CUDA graph (the NCCL all-gather of the
+totals inside it) and checks that it rewrites the same slices.  Rank 0 writes "ok"
 to the file named by argv[1] when they are identical.
 """
 
@@ -37,10 +39,26 @@ def main():
         grid = tack.UniformGrid(nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
         plan = SlabPlan(shape[2], world, rank)
         vals = workloads.generate("blobs", shape, plan.k0, plan.k1)
-        r = SlabEngine(grid, plan, [0.5]).run(vals)
+        eng = SlabEngine(grid, plan, [0.5])
+        r = eng.run(vals)
         part = {"points": r["points_field"].tensor.cpu().numpy(),
                 "conn": r["conn_field"].tensor.cpu().numpy(),
                 "counts": r["counts"], "bases": r["bases"]}
+        # The device-planned step captured in a CUDA graph, NCCL all-gather
+        # inside, replayed twice: the same slices.
+        pts = torch.zeros_like(r["points_field"].tensor)
+        conn = torch.zeros_like(r["conn_field"].tensor)
+        graph = eng.capture(vals, pts, conn)
+        for _ in range(2):
+            pts.zero_()
+            graph.replay()
+        torch.cuda.synchronize()
+        eng.check()
+        graph_ok = (torch.equal(pts.view(torch.int32), r["points_field"].tensor.view(torch.int32))
+                    and torch.equal(conn, r["conn_field"].tensor))
+        del graph
+        flags = [None] * world
+        dist.all_gather_object(flags, graph_ok)
         parts = [None] * world
         dist.all_gather_object(parts, part)
         if rank == 0:
@@ -48,7 +66,8 @@ def main():
             whole = workloads.generate("blobs", shape)
             ref = tack.flying_edges(tack.from_torch(whole), grid, 0.5)
             ok = (np.array_equal(conn, ref["conn"]) and
-                  np.array_equal(points.view(np.uint32), ref["points"].view(np.uint32)))
+                  np.array_equal(points.view(np.uint32), ref["points"].view(np.uint32)) and
+                  all(flags))
             with open(sys.argv[1], "w") as f:
                 f.write("ok\n" if ok else "mismatch\n")
         dist.barrier()
