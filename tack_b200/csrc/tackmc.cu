@@ -292,8 +292,8 @@ __device__ void lookback(uint32_t* flags, long long* agg, long long* incl,
 // K1: threshold the volume into node bitmasks (all isovalues, one read)
 // ------------------------------------------------------------------------
 //
-// A warp takes 1024 consecutive nodes (4 KiB) per step: eight coalesced
-// 512-byte float4 loads, issued before any use.  Four ballots per load give
+// A warp takes 1024 consecutive nodes (4 KiB): eight coalesced 512-byte
+// float4 loads, issued before any use.  Four ballots per load give
 // the "above" bits in lane-interleaved order; each lane assembles one 32-bit
 // word of node order and the warp stores 32 words (128 B) coalesced.
 //
@@ -310,65 +310,53 @@ __device__ __forceinline__ void store_summary(uint2* sums, int64_t ch, uint32_t 
 }
 
 __global__ void __launch_bounds__(kThreads)
-k_fe_threshold_v4(const float* __restrict__ v, int64_t n, IsoParams iso, int niso,
+k_fe_threshold_v4(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
                   uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
-                  uint2* __restrict__ sums, int64_t sums_stride) {
+                  uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks) {
+  // nfull = chunks with all 1024 nodes present; a ragged last chunk (if
+  // any) is done by k_fe_threshold_scalar.
   const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int64_t nchunks = (n + 1023) >> 10;
-  const float4* __restrict__ v4 = reinterpret_cast<const float4*>(v);
+  const int64_t ch = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
     const int t = threadIdx.x >> 3;
     if (t < niso) bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;  // padding
     if (t < niso && (threadIdx.x & 7) < 2)
       sums[t * sums_stride + nchunks + (threadIdx.x & 7)] = make_uint2(0u, 0u);
   }
-  for (int64_t ch = warp; ch < nchunks; ch += nwarps) {
-    const int64_t base = ch << 10;
-    float4 x[8];
-    if (base + 1024 <= n) {
+  if (ch >= nfull) return;  // whole warps only
+  const float4* __restrict__ v4 = reinterpret_cast<const float4*>(v) + (ch << 8);
+  float4 x[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) x[q] = __ldcs(v4 + (base >> 2) + q * 32 + lane);
-    } else {
+  for (int q = 0; q < 8; ++q) x[q] = __ldcs(v4 + q * 32 + lane);
+  const int64_t wi = (ch << 5) + lane;
+  const int sh = (lane & 3) * 8;
+  for (int t = 0; t < niso; ++t) {
+    const float th = iso.v[t];
+    uint32_t word = 0;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int64_t e = base + q * 128 + lane * 4;
-        x[q].x = e + 0 < n ? v[e + 0] : -INFINITY;
-        x[q].y = e + 1 < n ? v[e + 1] : -INFINITY;
-        x[q].z = e + 2 < n ? v[e + 2] : -INFINITY;
-        x[q].w = e + 3 < n ? v[e + 3] : -INFINITY;
-      }
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t b0 = __ballot_sync(0xffffffffu, x[q].x > th);
+      const uint32_t b1 = __ballot_sync(0xffffffffu, x[q].y > th);
+      const uint32_t b2 = __ballot_sync(0xffffffffu, x[q].z > th);
+      const uint32_t b3 = __ballot_sync(0xffffffffu, x[q].w > th);
+      if ((lane >> 2) == q)
+        word = spread8(b0 >> sh) | (spread8(b1 >> sh) << 1) |
+               (spread8(b2 >> sh) << 2) | (spread8(b3 >> sh) << 3);
     }
-    const int64_t wi = (ch << 5) + lane;
-    const int sh = (lane & 3) * 8;
-    for (int t = 0; t < niso; ++t) {
-      const float th = iso.v[t];
-      uint32_t word = 0;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const uint32_t b0 = __ballot_sync(0xffffffffu, x[q].x > th);
-        const uint32_t b1 = __ballot_sync(0xffffffffu, x[q].y > th);
-        const uint32_t b2 = __ballot_sync(0xffffffffu, x[q].z > th);
-        const uint32_t b3 = __ballot_sync(0xffffffffu, x[q].w > th);
-        if ((lane >> 2) == q)
-          word = spread8(b0 >> sh) | (spread8(b1 >> sh) << 1) |
-                 (spread8(b2 >> sh) << 2) | (spread8(b3 >> sh) << 3);
-      }
-      if (wi < nwords) bits[t * bits_stride + wi] = word;
-      store_summary(sums + t * sums_stride, ch, word, lane);
-    }
+    bits[t * bits_stride + wi] = word;
+    store_summary(sums + t * sums_stride, ch, word, lane);
   }
 }
 
-// Same result for a volume pointer that is not 16-byte aligned: 32 scalar
-// coalesced loads per warp step, one ballot per word.
+// Same result for a volume pointer that is not 16-byte aligned, and for the
+// ragged last chunk of any volume: 32 scalar coalesced loads per warp step,
+// one ballot per word.  Chunks first_chunk, first_chunk + 1, ... .
 __global__ void __launch_bounds__(kThreads)
 k_fe_threshold_scalar(const float* __restrict__ v, int64_t n, IsoParams iso, int niso,
                       uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
-                      uint2* __restrict__ sums, int64_t sums_stride) {
+                      uint2* __restrict__ sums, int64_t sums_stride, int64_t first_chunk) {
   const int lane = threadIdx.x & 31;
-  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t warp = first_chunk + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const int64_t nchunks = (n + 1023) >> 10;
   if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
@@ -2805,16 +2793,31 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int vec = (reinterpret_cast<uintptr_t>(scalar) % 16) == 0;
   const int64_t nchunks = (f.V + 1023) / 1024;
-  const int g = grid_for(nchunks, kThreads / 32, 8);
+  // One 1024-node chunk per warp, blocks in address order: the blocks in
+  // flight at any moment read one contiguous region of the volume, which
+  // streams measurably faster from HBM than a persistent grid-stride loop
+  // (6.9 vs 6.0 TB/s on a 4 GiB volume).
+  constexpr int kWarps = kThreads / 32;
   uint32_t* bits0 = v.iso[0].bits;
   uint2* sums0 = v.iso[0].sums;
-  if (vec)
-    k_fe_threshold_v4<<<g, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0, f.bits_stride,
-                                              f.nwords, sums0, f.sums_stride);
-  else
-    k_fe_threshold_scalar<<<g, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0, f.bits_stride,
-                                                  f.nwords, sums0, f.sums_stride);
-  TK_LAUNCHED();
+  const int64_t nfull = vec ? f.V / 1024 : 0;
+  if (nfull > 0) {
+    const int64_t gb = (nfull + kWarps - 1) / kWarps;
+    if (gb > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
+    k_fe_threshold_v4<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
+                                                         f.bits_stride, f.nwords, sums0,
+                                                         f.sums_stride, nchunks);
+    TK_LAUNCHED();
+  }
+  if (nfull < nchunks) {  // unaligned volume, or the ragged last chunk
+    const int64_t rest = nchunks - nfull;
+    const int64_t gb = (rest + kWarps - 1) / kWarps;
+    if (gb > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
+    k_fe_threshold_scalar<<<(unsigned)gb, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0,
+                                                             f.bits_stride, f.nwords, sums0,
+                                                             f.sums_stride, nfull);
+    TK_LAUNCHED();
+  }
   return TKMC_OK;
 }
 
