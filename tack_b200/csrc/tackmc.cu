@@ -427,7 +427,7 @@ struct FeIsoWs {
   uint32_t* work;       // active own rows
   uint32_t* ufirst;     // [R] index of each row's first unit (word-aligned rows)
   uint32_t* ucnt;       // [R] units of each row (word-aligned rows)
-  uint2* uslot;         // [R][kUnitSlots] {word, packed counts} of a row's first units
+  uint32_t* wcnt;       // [R][W] packed counts of each active word (word-aligned rows)
   FeUnit* units;        // units in (row, word) order, then a sentinel with the totals
   uint32_t* flags;      // [ntiles] (scan tiles of kScanRows rows)
   long long* super;     // [ntiles / kSuperTiles + 1][5] super-tile totals (word-aligned rows)
@@ -739,6 +739,29 @@ __device__ __forceinline__ int nth_set_bit(uint32_t m, int k) {
   return pos;
 }
 
+// Exclusive prefix of `x` over the lanes of the caller's run, where runs are
+// maximal sequences of lanes with equal `key` (keys of a run are contiguous).
+// *run_total receives the run's total in the run's last lane.
+__device__ __forceinline__ unsigned seg_excl(unsigned x, int key, unsigned* run_total,
+                                             bool* is_last) {
+  const int lane = threadIdx.x & 31;
+  unsigned incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  const int prev = __shfl_up_sync(0xffffffffu, key, 1);
+  const bool head = lane == 0 || prev != key;
+  const uint32_t hm = __ballot_sync(0xffffffffu, head);
+  const int first = 31 - __clz(hm & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u)));
+  const unsigned before = __shfl_sync(0xffffffffu, incl, first > 0 ? first - 1 : 0);
+  const unsigned base = first > 0 ? before : 0u;
+  *is_last = lane == 31 || ((hm >> (lane + 1)) & 1u);
+  *run_total = incl - base;
+  return incl - x - base;
+}
+
 // Word-aligned rows (L % 32 == 0): counts, offsets and the unit list.
 //
 // One thread per node row.  For each group of 32 words of its row the
@@ -863,12 +886,11 @@ __device__ __forceinline__ uint32_t count_word(const WordQuad& x, const RowQuad&
   return x0 | (y0 << 6) | (z0 << 12) | (t0 << 18);
 }
 
-constexpr int kUnitSlots = 8;  // units per row remembered between the count and offsets passes
 constexpr int kSuperTiles = 64;  // count tiles per super-tile total
 
 __device__ __forceinline__ void put_unit(FeUnit* units, int64_t cap, int64_t ui, uint32_t r,
                                          uint32_t w, const long long (&o)[4]) {
-  if (ui >= cap) return;  // the emit falls back to the row-wise kernel
+  if (ui >= cap) return;  // cannot happen: the list holds every word and the sentinel
   uint4* p = reinterpret_cast<uint4*>(units + ui);
   p[0] = make_uint4(r, w, (uint32_t)o[0], (uint32_t)o[1]);
   p[1] = make_uint4((uint32_t)o[2], 0u, (uint32_t)(unsigned long long)o[3],
@@ -886,26 +908,14 @@ __device__ __forceinline__ int owner_lane(unsigned v, unsigned e) {
   return lo;
 }
 
-// Lanes below `lane` in the run of equal keys that contains it (runs of a
-// key are contiguous).
-__device__ __forceinline__ uint32_t run_below_mask(int key) {
-  const int lane = threadIdx.x & 31;
-  const int prev = __shfl_up_sync(0xffffffffu, key, 1);
-  const bool head = lane == 0 || prev != key;
-  const uint32_t hm = __ballot_sync(0xffffffffu, head);
-  const uint32_t upto = lane == 31 ? 0xffffffffu : ((2u << lane) - 1u);
-  const int first = 31 - __clz(hm & upto);
-  return ((1u << lane) - 1u) & ~((1u << first) - 1u);
-}
-
-// K2a (word-aligned rows): per-row counts, activity masks and unit slots.
-// A warp owns 32 consecutive node rows.  Lane = row finds the row's
+// K2a (word-aligned rows): per-row counts, activity masks and per-word
+// counts.  A warp owns 32 consecutive node rows.  Lane = row finds the row's
 // candidate words; the warp then lists all candidates of its rows and counts
 // them 32 at a time, lane = candidate, so that the bit loads of 32 words are
-// in flight together.  Per-row sums go through shared-memory atomics; the
-// first kUnitSlots active words of each row are remembered (word index and
-// packed counts) for the offsets pass.  Each block also leaves its tile's
-// totals {X, Y, Z, T, units} for the tile scan.
+// in flight together.  Per-row sums go through shared-memory atomics; each
+// active word's packed counts are kept (wcnt) for the offsets pass.  Each
+// block also leaves its tile's totals {X, Y, Z, T, units} and adds them to
+// its super-tile's.
 __global__ void __launch_bounds__(kThreads)
 k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   __shared__ int s_ntri[256];
@@ -953,27 +963,21 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
         const RowQuad oq = row_quad(d, rbase + own);
         c = count_word(load_word_quad(Wk.bits, oq, w, W), oq, w, Li, d, mask, s_ntri);
       }
-      const bool active = c != 0u;
-      const int rl = warp * 32 + own;
-      if (active) {
+      if (c != 0u) {
+        const int rl = warp * 32 + own;
         atomicAdd(&s_cnt[0][rl], c & 63u);
         atomicAdd(&s_cnt[1][rl], (c >> 6) & 63u);
         atomicAdd(&s_cnt[2][rl], (c >> 12) & 63u);
         atomicAdd(&s_cnt[3][rl], c >> 18);
         atomicOr(&s_act[rl], 1u << (w & 31));
+        Wk.wcnt[(rbase + own) * W + w] = c;
       }
-      const uint32_t ab = __ballot_sync(0xffffffffu, active);
-      const uint32_t below = run_below_mask(ve ? own : -1);
-      const unsigned slot = s_nu[rl] + __popc(ab & below);
-      __syncwarp();
-      if (active) {
-        if (slot < kUnitSlots)
-          Wk.uslot[(rbase + own) * kUnitSlots + slot] = make_uint2((uint32_t)w, c);
-        atomicAdd(&s_nu[rl], 1u);
-      }
-      __syncwarp();
     }
-    if (valid) Wk.wact[r * d.AW + g] = s_act[tid];
+    __syncwarp();
+    if (valid) {
+      Wk.wact[r * d.AW + g] = s_act[tid];
+      s_nu[tid] += __popc(s_act[tid]);
+    }
     __syncwarp();
   }
   long long own5[5] = {0, 0, 0, 0, 0};
@@ -1003,25 +1007,25 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   }
 }
 
-// K2b (word-aligned rows): the first unit of each row, the units, the
-// totals, and -- only when the unit list overflowed, or when asked
-// (rows_only) -- the row offsets and the worklist of active own rows that the
-// row-wise emit kernel uses.  One thread per row, the same tiles as K2a.
-// The tile's prefix is the sum of the super-tile totals before its super-tile
+// K2b (word-aligned rows): the first unit of each row, the units and the
+// totals (rows_only: the row offsets instead, for tkmc_fe_row_offsets).  The
+// tile's prefix is the sum of the super-tile totals before its super-tile
 // and of the tile totals before it within its super-tile; the grand totals
-// are the sum of all super-tile totals.  No block waits for another.
+// are the sum of all super-tile totals; no block waits for another.  Lane =
+// row for the offsets, then the warp writes its rows' units 32 at a time,
+// lane = unit: the unit's word from the row's activity mask, its counts from
+// wcnt, its offsets from the row's running offsets plus a segmented prefix
+// over the batch.
 __global__ void __launch_bounds__(kThreads)
-k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t unit_cap,
-                   int rows_only) {
-  __shared__ int s_ntri[256];
+k_fe_offsets_units(FeDims d, FeWsAll ws, int64_t unit_cap, int rows_only) {
   __shared__ long long s_w[5][kThreads / 32];
   __shared__ long long s_pre[5], s_all[5];
-  __shared__ unsigned s_wbase[kThreads / 32];
+  __shared__ long long s_run[kThreads / 32][32][4];
   const FeIsoWs& Wk = ws.iso[blockIdx.y];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256; synced below
   const int64_t tile = blockIdx.x;
-  const int64_t r = tile * kThreads + tid;
+  const int64_t rbase = tile * kThreads + warp * 32;  // the warp's first row
+  const int64_t r = rbase + lane;
   const bool valid = r < d.R;
   if (warp < 5) {  // warp k sums value k of the tile's prefix and of the grand total
     const int k = warp;
@@ -1072,17 +1076,15 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64
       if (w2 < warp) before += s_w[t][w2];
     ex[t] = s_pre[t] + before + inc[t] - own[t];
   }
-  // The row-wise emit kernel runs instead when the units do not fit.
-  const bool overflow = s_all[4] + 1 > unit_cap;
-  const bool rows = overflow || rows_only;
-  if (valid) {
-    if (rows) {
+  if (rows_only) {
+    if (valid) {
       longlong2* dst = reinterpret_cast<longlong2*>(Wk.rowoff + r * 4);
       dst[0] = make_longlong2(ex[0], ex[1]);
       dst[1] = make_longlong2(ex[2], ex[3]);
     }
+    return;
   }
-  if (valid && !rows_only) {
+  if (valid) {
     Wk.ufirst[r] = (uint32_t)ex[4];
     // Own totals: the offsets of the first ghost row.
     if (r == d.n_own_rows) {
@@ -1104,53 +1106,64 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64
       put_unit(Wk.units, unit_cap, s_all[4], (uint32_t)d.R, 0u, o);
     }
   }
-  if (valid && !rows_only && !overflow && nU) {
-    long long o[4] = {ex[0], ex[1], ex[2], ex[3]};
-    int64_t ui = ex[4];
-    if (nU <= kUnitSlots) {
-      // The row's slots are 64 contiguous bytes: load what is used at once.
-      const uint4* sp = reinterpret_cast<const uint4*>(Wk.uslot + r * kUnitSlots);
-      uint4 sv[kUnitSlots / 2];
+  // ---- the warp's units, lane = unit ----
 #pragma unroll
-      for (int i = 0; i < kUnitSlots / 2; ++i)
-        sv[i] = (unsigned)(2 * i) < nU ? __ldcg(sp + i) : make_uint4(0u, 0u, 0u, 0u);
+  for (int t = 0; t < 4; ++t) s_run[warp][lane][t] = ex[t];
+  unsigned pre = nU;
 #pragma unroll
-      for (int i = 0; i < kUnitSlots; ++i) {
-        if ((unsigned)i >= nU) break;
-        const uint32_t sw = (i & 1) ? sv[i >> 1].z : sv[i >> 1].x;
-        const uint32_t sc = (i & 1) ? sv[i >> 1].w : sv[i >> 1].y;
-        put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, sw, o);
-        o[0] += sc & 63u;
-        o[1] += (sc >> 6) & 63u;
-        o[2] += (sc >> 12) & 63u;
-        o[3] += sc >> 18;
-      }
-    } else {  // long active rows: count their active words again
-      const RowQuad q = row_quad(d, r);
-      for (int g = 0; g < d.AW; ++g) {
-        uint32_t act = __ldcg(Wk.wact + r * d.AW + g);
-        while (act) {
-          const int w = 32 * g + __ffs(act) - 1;
-          act &= act - 1u;
-          const uint32_t cw = count_word(load_word_quad(Wk.bits, q, w, d.W), q, w, (int)d.L,
-                                         d, mask, s_ntri);
-          put_unit(Wk.units, unit_cap, ui++, (uint32_t)r, (uint32_t)w, o);
-          o[0] += cw & 63u;
-          o[1] += (cw >> 6) & 63u;
-          o[2] += (cw >> 12) & 63u;
-          o[3] += cw >> 18;
-        }
-      }
-    }
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_up_sync(0xffffffffu, pre, o);
+    if (lane >= o) pre += y;
   }
-  // Worklist of own rows with any output, for the row-wise emit kernel.
-  const bool act_row = overflow && !rows_only && valid && r < d.n_own_rows && nU != 0;
-  const uint32_t bal = __ballot_sync(0xffffffffu, act_row);
-  if (lane == 0 && bal)
-    s_wbase[warp] = (unsigned)atomicAdd((unsigned long long*)(Wk.info + 8),
-                                        (unsigned long long)__popc(bal));
+  const unsigned NU = __shfl_sync(0xffffffffu, pre, 31);
+  pre -= nU;
+  const long long ufirst = ex[4];
   __syncwarp();
-  if (act_row) Wk.work[s_wbase[warp] + __popc(bal & ((1u << lane) - 1u))] = (uint32_t)r;
+  for (unsigned b0 = 0; b0 < NU; b0 += 32) {
+    const unsigned e = b0 + lane;
+    const bool ve = e < NU;
+    const int own_l = owner_lane(pre, ve ? e : NU - 1);
+    const unsigned opre = __shfl_sync(0xffffffffu, pre, own_l);
+    const long long ou = __shfl_sync(0xffffffffu, ufirst, own_l);
+    const int64_t orow = rbase + own_l;
+    int w = 0;
+    uint32_t cw = 0;
+    if (ve) {
+      int k = (int)(e - opre);  // k-th active word of the row
+      for (int i = 0; i < d.AW; ++i) {
+        const uint32_t m = __ldcg(Wk.wact + orow * d.AW + i);
+        const int n = __popc(m);
+        if (k < n) {
+          w = 32 * i + nth_set_bit(m, k);
+          break;
+        }
+        k -= n;
+      }
+      cw = __ldcg(Wk.wcnt + orow * d.W + w);
+    }
+    const int key = ve ? own_l : -1;
+    unsigned tA, tB;
+    bool last;
+    const unsigned xA = (cw & 63u) | (((cw >> 6) & 63u) << 11);
+    const unsigned xB = ((cw >> 12) & 63u) | ((cw >> 18) << 11);
+    const unsigned eA = seg_excl(xA, key, &tA, &last);
+    const unsigned eB = seg_excl(xB, key, &tB, &last);
+    if (ve) {
+      const long long* rr = s_run[warp][own_l];
+      const long long o[4] = {rr[0] + (eA & 2047u), rr[1] + (eA >> 11), rr[2] + (eB & 2047u),
+                              rr[3] + (eB >> 11)};
+      put_unit(Wk.units, unit_cap, ou + (long long)(e - opre), (uint32_t)orow, (uint32_t)w, o);
+    }
+    __syncwarp();
+    if (ve && last) {
+      long long* rr = s_run[warp][own_l];
+      rr[0] += tA & 2047u;
+      rr[1] += tA >> 11;
+      rr[2] += tB & 2047u;
+      rr[3] += tB >> 11;
+    }
+    __syncwarp();
+  }
 }
 
 // K2b: single-pass (decoupled look-back) exclusive scan of the row counts
@@ -1645,29 +1658,6 @@ __device__ __forceinline__ int find_slot(const uint32_t* base, int stride, int f
   return lo;
 }
 
-// Exclusive prefix of `x` over the lanes of the caller's run, where runs are
-// maximal sequences of lanes with equal `key` (keys of a run are contiguous).
-// *run_total receives the run's total in the run's last lane.
-__device__ __forceinline__ unsigned seg_excl(unsigned x, int key, unsigned* run_total,
-                                             bool* is_last) {
-  const int lane = threadIdx.x & 31;
-  unsigned incl = x;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  const int prev = __shfl_up_sync(0xffffffffu, key, 1);
-  const bool head = lane == 0 || prev != key;
-  const uint32_t hm = __ballot_sync(0xffffffffu, head);
-  const int first = 31 - __clz(hm & (lane == 31 ? 0xffffffffu : ((2u << lane) - 1u)));
-  const unsigned before = __shfl_sync(0xffffffffu, incl, first > 0 ? first - 1 : 0);
-  const unsigned base = first > 0 ? before : 0u;
-  *is_last = lane == 31 || ((hm >> (lane + 1)) & 1u);
-  *run_total = incl - base;
-  return incl - x - base;
-}
-
 __device__ __forceinline__ long long ld_i64(const uint32_t* p) {
   return (long long)(((unsigned long long)p[1] << 32) | p[0]);
 }
@@ -1698,14 +1688,12 @@ __device__ __forceinline__ uint32_t row_word_next(const uint32_t* __restrict__ b
 }
 
 __global__ void __launch_bounds__(kThreads, 3)
-k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
+k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
   extern __shared__ uint32_t k3_smem[];
   __shared__ uint64_t s_case[256];
   EmitSmem& S = *reinterpret_cast<EmitSmem*>(k3_smem);
   const int isoi = blockIdx.y;
   const FeIsoWs& W = ws.iso[isoi];
-  // Word-aligned rows whose unit list fit are emitted by k_fe_emit_units.
-  if (unit_cap > 0 && *((volatile long long*)(W.info + 11)) + 1 <= unit_cap) return;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_tris[tid];
   __syncthreads();
@@ -2030,7 +2018,7 @@ __device__ __forceinline__ int find_rec(const uint32_t* recs, int field, unsigne
 }
 
 __global__ void __launch_bounds__(kThreads, 4)
-k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
+k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
   __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
   __shared__ long long s_tri[kThreads / 32][32];
@@ -2039,8 +2027,6 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A, int64_t unit_cap) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_groups[tid];  // kThreads == 256
   __syncthreads();
-  const long long n_all = *((volatile long long*)(W.info + 11));
-  if (n_all + 1 > unit_cap) return;  // the unit list overflowed: k_fe_emit_words runs instead
   const long long n_own = *((volatile long long*)(W.info + 12));
   uint32_t* U = s_rec[warp];
   long long* TR = s_tri[warp];
@@ -2449,7 +2435,7 @@ struct FeLayout {
   size_t k2_smem;   // dynamic shared memory of the count kernel (rows not word-aligned)
   int64_t V, nwords, bits_stride, nchunks, sums_stride;
   int64_t unit_cap;  // units (incl. the sentinel) the workspace holds; 0: rows not word-aligned
-  size_t off_units, off_ufirst, off_ucnt, off_uslot, off_super;
+  size_t off_units, off_ufirst, off_ucnt, off_wcnt, off_super;
   int64_t super_stride;
   size_t off_bits, off_sums, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
@@ -2498,9 +2484,8 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.bits_stride = (int64_t)align_up((size_t)(f.nwords + 8), 64);
   f.nchunks = (f.V + 1023) / 1024;
   f.sums_stride = (int64_t)align_up((size_t)(f.nchunks + 2), 32);
-  // Unit list: room for one word in eight of the volume to have output, plus
-  // the sentinel; a surface with more units is emitted row-wise instead.
-  f.unit_cap = aligned ? f.nwords / 8 + 1024 : 0;
+  // Unit list: room for every word of the volume, plus the sentinel.
+  f.unit_cap = aligned ? f.nwords + 1 : 0;
   if (f.nwords > 0xffffffffLL) return false;  // unit and row indices are uint32
   size_t o = 0;
   f.off_info = o;   o = align_up(o + (size_t)niso * 16 * 8, 256);
@@ -2520,7 +2505,7 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.off_sums = o;   o = align_up(o + (size_t)niso * f.sums_stride * 8, 256);
   f.off_ufirst = o; o = align_up(o + (aligned ? (size_t)niso * d.R * 4 : 0), 256);
   f.off_ucnt = o;   o = align_up(o + (aligned ? (size_t)niso * d.R * 4 : 0), 256);
-  f.off_uslot = o;  o = align_up(o + (aligned ? (size_t)niso * d.R * kUnitSlots * 8 : 0), 256);
+  f.off_wcnt = o;   o = align_up(o + (aligned ? (size_t)niso * f.nwords * 4 : 0), 256);
   f.off_units = o;  o = align_up(o + (size_t)niso * f.unit_cap * sizeof(FeUnit), 256);
   f.total = o;
   *out = f;
@@ -2546,7 +2531,7 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
     w.ufirst = reinterpret_cast<uint32_t*>(b + f.off_ufirst) + (size_t)q * f.d.R;
     w.units = reinterpret_cast<FeUnit*>(b + f.off_units) + (size_t)q * f.unit_cap;
     w.ucnt = reinterpret_cast<uint32_t*>(b + f.off_ucnt) + (size_t)q * f.d.R;
-    w.uslot = reinterpret_cast<uint2*>(b + f.off_uslot) + (size_t)q * f.d.R * kUnitSlots;
+    w.wcnt = reinterpret_cast<uint32_t*>(b + f.off_wcnt) + (size_t)q * f.nwords;
     w.info = reinterpret_cast<long long*>(b + f.off_info) + (size_t)q * 16;
   }
   return a;
@@ -2836,7 +2821,7 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
     const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
     k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
     TK_LAUNCHED();
-    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, mask, f.unit_cap, 0);
+    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, f.unit_cap, 0);
     TK_LAUNCHED();
     return TKMC_OK;
   }
@@ -2883,7 +2868,7 @@ int tkmc_fe_row_offsets(int64_t nx, int64_t ny, int64_t nz, int niso, int iso,
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((f.d.L & 31) == 0) {  // word-aligned rows keep offsets per unit: fill the row table now
     k_fe_offsets_units<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
-        f.d, v, nullptr, f.unit_cap, 1);
+        f.d, v, f.unit_cap, 1);
     TK_LAUNCHED();
   }
   TK_CUDA(cudaMemcpyAsync(out, v.iso[iso].rowoff, (size_t)f.d.R * 4 * sizeof(long long),
@@ -2960,14 +2945,14 @@ static int fe_emit_impl(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   if (f.d.AW <= kMaxAW) {
     const size_t smem = sizeof(EmitSmem);
     if ((rc = ensure_smem(k_fe_emit_words, smem, g_smem_emit_words))) return rc;
-    if (f.unit_cap > 0) {
+    if (f.unit_cap > 0) {  // word-aligned rows: the unit list
       k_fe_emit_units<<<dim3((unsigned)(sm_count() * 8), (unsigned)niso), kThreads, 0, st>>>(
-          f.d, v, A, f.unit_cap);
+          f.d, v, A);
       TK_LAUNCHED();
+      return TKMC_OK;
     }
     const int g = grid_for(f.d.n_own_rows, kThreads, 3);
-    k_fe_emit_words<<<dim3((unsigned)g, (unsigned)niso), kThreads, smem, st>>>(f.d, v, A,
-                                                                              f.unit_cap);
+    k_fe_emit_words<<<dim3((unsigned)g, (unsigned)niso), kThreads, smem, st>>>(f.d, v, A);
   } else {
     const int G = 32 >> f.d.logS3;
     const int g = grid_for(f.d.n_own_rows, (kThreads / 32) * G, 8);

@@ -51,10 +51,10 @@ def test_workspace_sizes():
     b = lib.tkmc_fe_workspace_bytes(63, 63, 63, 4)
     c = lib.tkmc_fe_workspace_bytes(1023, 1023, 1023, 1)
     assert 0 < a < b < c
-    # 1024^3: bitmask 128 MiB + row offsets 32 MiB + unit list (one word in
-    # eight: 128 MiB) + unit slots 64 MiB + row counts 16 MiB + word
-    # summaries, activity masks, row lists (~24 MiB)
-    assert 380 << 20 < c < 400 << 20
+    # 1024^3: unit list (32 B for every 32-node word: 1 GiB) + bitmask 128 MiB
+    # + per-word counts 128 MiB + row offsets 32 MiB + row counts 16 MiB +
+    # word summaries, activity masks, row lists (~24 MiB)
+    assert 1300 << 20 < c < 1400 << 20
     assert lib.tkmc_fe_workspace_bytes(-1, 4, 4, 1) == 0
     assert lib.tkmc_fe_workspace_bytes(4, 4, 4, 0) == 0
     assert lib.tkmc_fe_workspace_bytes(4, 4, 4, 9) == 0

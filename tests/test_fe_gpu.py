@@ -227,10 +227,10 @@ def test_long_rows_match_oracle(tack, oracle, shape):
 
 @pytest.mark.parametrize("shape,density", [((255, 127, 30), "noise"), ((127, 63, 40), "smooth"),
                                            ((2047, 6, 5), "smooth")])
-def test_word_aligned_rows_units_and_fallback(tack, oracle, shape, density):
-    """Rows of a multiple of 32 nodes take the unit-list path.  White noise
-    makes nearly every word active, more units than the workspace's unit list
-    holds: the row-wise emit kernel must take over with the same result."""
+def test_word_aligned_rows_unit_list(tack, oracle, shape, density):
+    """Rows of a multiple of 32 nodes take the unit-list path: white noise
+    (nearly every word active, rows with more active words than a warp's
+    batch), smooth fields and long rows."""
     nx, ny, nz = shape
     assert (nx + 1) % 32 == 0
     rng = np.random.default_rng(nx + ny)
