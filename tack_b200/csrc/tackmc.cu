@@ -348,6 +348,43 @@ k_fe_threshold_v4(const float* __restrict__ v, int64_t nfull, IsoParams iso, int
   }
 }
 
+// Several isovalues: lane l loads nodes l, 32 + l, ..., 992 + l of the chunk
+// (32 coalesced 128-byte loads per warp), so that each ballot is directly
+// the bit word of 32 consecutive nodes and no interleave is needed -- per
+// isovalue 32 compares, 32 ballots and 32 selects instead of the float4
+// layout's ballots plus four-way interleave, which leaves the kernel issue
+// bound once it runs for several isovalues.  Full chunks only, like v4.
+__global__ void __launch_bounds__(kThreads, 5)
+k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
+                     uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
+                     uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ch = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
+    const int t = threadIdx.x >> 3;
+    if (t < niso) bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;  // padding
+    if (t < niso && (threadIdx.x & 7) < 2)
+      sums[t * sums_stride + nchunks + (threadIdx.x & 7)] = make_uint2(0u, 0u);
+  }
+  if (ch >= nfull) return;  // whole warps only
+  const float* __restrict__ p = v + (ch << 10) + lane;
+  float x[32];
+#pragma unroll
+  for (int q = 0; q < 32; ++q) x[q] = __ldcs(p + 32 * q);
+  const int64_t wi = (ch << 5) + lane;
+  for (int t = 0; t < niso; ++t) {
+    const float th = iso.v[t];
+    uint32_t word = 0;
+#pragma unroll
+    for (int q = 0; q < 32; ++q) {
+      const uint32_t b = __ballot_sync(0xffffffffu, x[q] > th);
+      word = lane == q ? b : word;
+    }
+    bits[t * bits_stride + wi] = word;
+    store_summary(sums + t * sums_stride, ch, word, lane);
+  }
+}
+
 // Same result for a volume pointer that is not 16-byte aligned, and for the
 // ragged last chunk of any volume: 32 scalar coalesced loads per warp step,
 // one ballot per word.  Chunks first_chunk, first_chunk + 1, ... .
@@ -2785,13 +2822,20 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   constexpr int kWarps = kThreads / 32;
   uint32_t* bits0 = v.iso[0].bits;
   uint2* sums0 = v.iso[0].sums;
-  const int64_t nfull = vec ? f.V / 1024 : 0;
+  // Full chunks: float4 loads for one isovalue (16-byte-aligned volumes),
+  // one-word ballots for several (any alignment).
+  const int64_t nfull = (vec || niso > 1) ? f.V / 1024 : 0;
   if (nfull > 0) {
     const int64_t gb = (nfull + kWarps - 1) / kWarps;
     if (gb > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
-    k_fe_threshold_v4<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
-                                                         f.bits_stride, f.nwords, sums0,
-                                                         f.sums_stride, nchunks);
+    if (niso == 1)
+      k_fe_threshold_v4<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
+                                                           f.bits_stride, f.nwords, sums0,
+                                                           f.sums_stride, nchunks);
+    else
+      k_fe_threshold_multi<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
+                                                              f.bits_stride, f.nwords, sums0,
+                                                              f.sums_stride, nchunks);
     TK_LAUNCHED();
   }
   if (nfull < nchunks) {  // unaligned volume, or the ragged last chunk
