@@ -141,7 +141,7 @@ class ClockSampler:
 
 # ---------------------------------------------------------------- reference arm
 
-def cpu_sample_rate(volume_host_planes, shape, k0, nthreads, min_seconds, max_calls=50):
+def cpu_sample_rate(volume_host_planes, shape, k0, isos, nthreads, min_seconds, max_calls=50):
     """Oracle flying_edges on a z-slab; returns (Gcells/s, per-call seconds, cells)."""
     from oracle import oracle
     nx, ny, _ = shape
@@ -152,7 +152,7 @@ def cpu_sample_rate(volume_host_planes, shape, k0, nthreads, min_seconds, max_ca
     t_start = time.perf_counter()
     while True:
         t0 = time.perf_counter()
-        oracle.flying_edges(volume_host_planes, g, 0.5, nthreads=nthreads)
+        oracle.flying_edges_isovalues(volume_host_planes, g, isos, nthreads=nthreads)
         times.append(time.perf_counter() - t0)
         if (time.perf_counter() - t_start >= min_seconds and len(times) >= 3) or \
                 len(times) >= max_calls:
@@ -184,7 +184,7 @@ def run_reference(args):
     nthreads = oracle.num_threads(0)
     # Size the slab so that warmup + steps fit in about two minutes.
     calib, k0 = host_slab(args, shape, 8, device)
-    rate, _, _ = cpu_sample_rate(calib, shape, k0, nthreads, 0.0, max_calls=2)
+    rate, _, _ = cpu_sample_rate(calib, shape, k0, cfg["isovalues"], nthreads, 0.0, max_calls=2)
     budget = 120.0 / max(1, args.steps + args.warmup)
     cells_per_plane = (shape[0] - 1) * (shape[1] - 1)
     planes = int(np.clip(budget * rate * 1e9 / cells_per_plane, 2, min(128, shape[2])))
@@ -193,11 +193,11 @@ def run_reference(args):
     g = oracle.Grid(shape[0] - 1, shape[1] - 1, nz_cells, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0)
     cells = cells_per_plane * nz_cells
     for _ in range(args.warmup):
-        oracle.flying_edges(vol, g, cfg["isovalues"][0], nthreads=nthreads)
+        oracle.flying_edges_isovalues(vol, g, cfg["isovalues"], nthreads=nthreads)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        oracle.flying_edges(vol, g, cfg["isovalues"][0], nthreads=nthreads)
+        oracle.flying_edges_isovalues(vol, g, cfg["isovalues"], nthreads=nthreads)
         times.append(time.perf_counter() - t0)
     total = sum(times)
     value = cells * args.steps / total / 1e9
@@ -338,6 +338,12 @@ def main():
     total_points = int(bases["totals"][:, 0].sum())
     total_tris = int(bases["totals"][:, 1].sum())
 
+    # ---- next filter on the same surface: vertex normals (one GPU) --------
+    normals = None
+    if world == 1 and own_p > 0 and own_t > 0:
+        normals = time_normals(tack, torch, pts_buf[:own_p * 3], conn_buf[:own_t * 3], own_p,
+                               own_t, stream)
+
     # ---- e2e through the public API, host buffers -------------------------
     e2e = None
     if not args.no_e2e and args.e2e_steps > 0:
@@ -353,7 +359,7 @@ def main():
         planes = min(64, nzn)
         k0 = max(0, nzn // 2 - planes // 2)
         slab = vol.view(nzn, nyn, nxn)[k0:k0 + planes].reshape(-1).cpu().numpy()
-        rate, t_call, scells = cpu_sample_rate(slab, shape, k0, nthreads, args.cpu_seconds)
+        rate, t_call, scells = cpu_sample_rate(slab, shape, k0, isos, nthreads, args.cpu_seconds)
         cpu = {"value": rate, "unit": "Gcells/s", "cores": nthreads, "kind": "port",
                "sample": (f"node planes [{k0},{k0 + planes}) of the same volume "
                           f"({scells} cells), median of repeated calls over "
@@ -400,6 +406,7 @@ def main():
             "kernels_ms": {"k1_threshold": k1, "k2_count_scan": k2,
                            "totals_gather_plan": host, "k3_emit": k3},
             "outputs": {"points": total_points, "triangles": total_tris},
+            "compute_normals": normals,
             "gpu_launches": int(launches),
             "gpu_launches_per_step": launches / K,
             "cuda_graph": True,
@@ -411,6 +418,26 @@ def main():
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def time_normals(tack, torch, points, conn, n_pts, n_tris, stream, reps=20):
+    """tack_b200.compute_normals on the bench's surface: device time per call
+    (CUDA events) and its algorithmic bytes (read 12 B per triangle of conn
+    and 36 B of vertex positions, write 12 B per normal)."""
+    for _ in range(3):
+        tack.compute_normals(points, conn, n_pts, n_tris)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        tack.compute_normals(points, conn, n_pts, n_tris)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    nbytes = 48.0 * n_tris + 12.0 * n_pts
+    return {"ms": ms, "gtris_per_s": n_tris / (ms * 1e-3) / 1e9,
+            "algorithmic_gbs": nbytes / (ms * 1e-3) / 1e9,
+            "note": "deterministic 64-bit fixed-point sums; includes one host sync (id check)"}
 
 
 def ctypes_f32(vals):

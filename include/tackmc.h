@@ -107,6 +107,25 @@ int tkmc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive,
 int tkmc_scan_i32_noalloc(const int32_t* in, int32_t* out, int64_t n,
                           int inclusive, int64_t* total, void* stream);
 
+/* ---- vertex normals ------------------------------------------------------ */
+
+/* Workspace for tkmc_compute_normals over n_pts points. */
+size_t tkmc_normals_workspace_bytes(int64_t n_pts);
+
+/* Smooth vertex normals of a triangle mesh: each triangle's area-weighted
+ * face normal cross(v1 - v0, v2 - v0) (f32, the reference's operation order)
+ * is added to its three vertices, then every vertex sum longer than 1e-10 is
+ * normalised (shorter ones are left as summed).  points f32 [n_pts*3]
+ * interleaved, conn int32 [n_tris*3], normals f32 [n_pts*3] out.  The sums
+ * are 64-bit fixed point, so the result does not depend on the order of the
+ * additions (the reference's f32 atomics do); a vertex of a face whose
+ * normal is not finite gets NaN.  Point ids outside [0, n_pts) return
+ * TKMC_ERR_INVALID_ARG.  Synchronises `stream` once (the id check).
+ * Replaces: compute_normals.py:16-90 (compute_normals). */
+int tkmc_compute_normals(const float* points, const int32_t* conn, int64_t n_pts,
+                         int64_t n_tris, void* workspace, size_t workspace_bytes,
+                         float* normals, void* stream);
+
 /* ---- flying edges (merged-point marching cubes) ------------------------- */
 /*
  * Grid: nx, ny, nz cells; (nx+1)*(ny+1)*(nz+1) f32 node values, i fastest,

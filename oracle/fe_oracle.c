@@ -412,4 +412,40 @@ void orc_reduce_f32(const float* v, int64_t n, double out4[4]) {
   out4[3] = (double)nan;
 }
 
+/* ---- compute_normals (compute_normals.py:16-90) ------------------------ */
+/* Serial restatement: triangles in order, each area-weighted face normal
+ * added to its three vertices in f32 (the reference adds them with atomics,
+ * so its order, and its last-bit rounding, varies), then every vertex with
+ * length > 1e-10 scaled by 1/length in f32. */
+void orc_compute_normals(const float* p, const int32_t* conn, int64_t n_pts, int64_t n_tris,
+                         float* out) {
+  for (int64_t i = 0; i < 3 * n_pts; ++i) out[i] = 0.0f;
+  for (int64_t t = 0; t < n_tris; ++t) {
+    const int64_t i0 = conn[3 * t], i1 = conn[3 * t + 1], i2 = conn[3 * t + 2];
+    const float e1x = p[3 * i1] - p[3 * i0], e1y = p[3 * i1 + 1] - p[3 * i0 + 1],
+                e1z = p[3 * i1 + 2] - p[3 * i0 + 2];
+    const float e2x = p[3 * i2] - p[3 * i0], e2y = p[3 * i2 + 1] - p[3 * i0 + 1],
+                e2z = p[3 * i2 + 2] - p[3 * i0 + 2];
+    const float nx = e1y * e2z - e1z * e2y;
+    const float ny = e1z * e2x - e1x * e2z;
+    const float nz = e1x * e2y - e1y * e2x;
+    const int64_t ids[3] = {i0, i1, i2};
+    for (int v = 0; v < 3; ++v) {
+      out[3 * ids[v]] += nx;
+      out[3 * ids[v] + 1] += ny;
+      out[3 * ids[v] + 2] += nz;
+    }
+  }
+  for (int64_t i = 0; i < n_pts; ++i) {
+    const float x = out[3 * i], y = out[3 * i + 1], z = out[3 * i + 2];
+    const float len = sqrtf(x * x + y * y + z * z);
+    if (len > 1.0e-10f) {
+      const float inv = 1.0f / len;
+      out[3 * i] = x * inv;
+      out[3 * i + 1] = y * inv;
+      out[3 * i + 2] = z * inv;
+    }
+  }
+}
+
 int orc_num_threads(int nthreads) { return resolve_threads(nthreads); }

@@ -78,6 +78,8 @@ def lib():
         L.orc_scan_i32.argtypes = [P, P, I64, I]
         L.orc_scan_i32.restype = I64
         L.orc_reduce_f32.argtypes = [P, I64, P]
+        L.orc_compute_normals.argtypes = [P, P, I64, I64, P]
+        L.orc_compute_normals.restype = None
         L.orc_num_threads.argtypes = [I]
         L.orc_num_threads.restype = I
         for name in ("orc_fe_count_edges_xyz", "orc_fe_count_rows", "orc_fe_emit_points_xyz",
@@ -280,3 +282,14 @@ def reduce(values):
     out = np.zeros(4, np.float64)
     lib().orc_reduce_f32(_ptr(a), a.size, _ptr(out))
     return float(out[0]), float(out[1]), float(out[2]), int(out[3])
+
+
+def compute_normals(points, conn):
+    """Vertex normals of a triangle mesh (compute_normals.py:16-90): f32
+    (n_pts, 3).  points (n_pts, 3) f32, conn (n_tris, 3) int32."""
+    p = np.ascontiguousarray(points, np.float32).reshape(-1)
+    c = np.ascontiguousarray(conn, np.int32).reshape(-1)
+    n_pts, n_tris = p.size // 3, c.size // 3
+    out = np.zeros(3 * n_pts, np.float32)
+    lib().orc_compute_normals(_ptr(p), _ptr(c), n_pts, n_tris, _ptr(out))
+    return out.reshape(-1, 3)

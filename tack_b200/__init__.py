@@ -13,7 +13,8 @@ libtackmc.so do all compute; PyTorch provides device memory, streams and
 """
 
 from . import algorithms  # noqa: F401
-from .algorithms import UniformGrid, flying_edges, flying_edges_multiblock  # noqa: F401
+from .algorithms import (UniformGrid, compute_normals, flying_edges,  # noqa: F401
+                         flying_edges_multiblock)
 from .field import (Field, ScalarType, f32, f64, field, field_from_ptr,  # noqa: F401
                     from_torch, i32, i64, reduce_f32, u8)
 from .runtime import cuda, current_device, init  # noqa: F401

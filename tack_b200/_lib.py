@@ -37,6 +37,8 @@ SIGNATURES = {
     "tkmc_scan_workspace_bytes": (_SZ, [_I64]),
     "tkmc_scan_i32": (_I, [_P, _P, _I64, _I, _P, _SZ, _P, _P]),
     "tkmc_scan_i32_noalloc": (_I, [_P, _P, _I64, _I, _P, _P]),
+    "tkmc_normals_workspace_bytes": (_SZ, [_I64]),
+    "tkmc_compute_normals": (_I, [_P, _P, _I64, _I64, _P, _SZ, _P, _P]),
     "tkmc_fe_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I]),
     "tkmc_fe_emit_dev": (_I, [_P, _I64, _I64, _I64, _I, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P,
                               _I64, _P, _I64, _P]),

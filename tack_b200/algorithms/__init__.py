@@ -1,9 +1,11 @@
-"""Algorithms on device fields: the flying-edges isosurface and its helpers.
+"""Algorithms on device fields: the flying-edges isosurface, its helpers, and
+vertex normals of the surface.
 
 Mirrors the names tack exports from ``tack.algorithms`` for this path
 (packages/tack-core/src/tack/algorithms/__init__.py:29-76).
 """
 
+from .compute_normals import compute_normals  # noqa: F401
 from .flying_edges import (MCTables, UniformGrid, flying_edges,  # noqa: F401
                            flying_edges_multiblock)
 from .marching_cubes import classify_cells  # noqa: F401

@@ -2306,6 +2306,138 @@ __global__ void k_fe_clear_capacity_error(FeWsAll ws, int niso) {
 }
 
 // ------------------------------------------------------------------------
+// vertex normals (compute_normals.py:16-90)
+// ------------------------------------------------------------------------
+//
+// The reference scatters every triangle's area-weighted face normal into its
+// three vertices with f32 atomics, whose order -- and so whose rounding --
+// changes from run to run.  Here the same face normals (same f32 operation
+// order, no contraction) are added as 64-bit fixed point: integer addition
+// is associative, so the sums do not depend on the order, and they keep
+// about 58 bits below the largest face normal instead of f32's 24.  The
+// scale is a power of two from a first pass over the faces: the largest
+// |component| times 2^kNormValence must stay below 2^62.
+constexpr int kNormValence = 6;  // a vertex may sum up to 64 faces of the largest size
+
+__device__ __forceinline__ void face_normal(const float* __restrict__ p, const int32_t* __restrict__ conn,
+                                            int64_t t, int32_t* i0, int32_t* i1, int32_t* i2,
+                                            float* nx, float* ny, float* nz) {
+  *i0 = __ldg(conn + 3 * t);
+  *i1 = __ldg(conn + 3 * t + 1);
+  *i2 = __ldg(conn + 3 * t + 2);
+  const float v0x = __ldg(p + 3 * (int64_t)*i0), v0y = __ldg(p + 3 * (int64_t)*i0 + 1),
+              v0z = __ldg(p + 3 * (int64_t)*i0 + 2);
+  const float v1x = __ldg(p + 3 * (int64_t)*i1), v1y = __ldg(p + 3 * (int64_t)*i1 + 1),
+              v1z = __ldg(p + 3 * (int64_t)*i1 + 2);
+  const float v2x = __ldg(p + 3 * (int64_t)*i2), v2y = __ldg(p + 3 * (int64_t)*i2 + 1),
+              v2z = __ldg(p + 3 * (int64_t)*i2 + 2);
+  const float e1x = __fsub_rn(v1x, v0x), e1y = __fsub_rn(v1y, v0y), e1z = __fsub_rn(v1z, v0z);
+  const float e2x = __fsub_rn(v2x, v0x), e2y = __fsub_rn(v2y, v0y), e2z = __fsub_rn(v2z, v0z);
+  *nx = __fsub_rn(__fmul_rn(e1y, e2z), __fmul_rn(e1z, e2y));
+  *ny = __fsub_rn(__fmul_rn(e1z, e2x), __fmul_rn(e1x, e2z));
+  *nz = __fsub_rn(__fmul_rn(e1x, e2y), __fmul_rn(e1y, e2x));
+}
+
+// Pass 1: the largest |face normal component| (f32 bits; non-negative
+// floats order like their bits) and a flag for ids out of range.
+__global__ void __launch_bounds__(kThreads)
+k_normals_max(const float* __restrict__ p, const int32_t* __restrict__ conn, int64_t n_pts,
+              int64_t n_tris, unsigned* __restrict__ maxbits, unsigned* __restrict__ bad) {
+  float m = 0.f;
+  unsigned badid = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_tris; t += stride) {
+    const int32_t a = __ldg(conn + 3 * t), b = __ldg(conn + 3 * t + 1), c = __ldg(conn + 3 * t + 2);
+    if (a < 0 || b < 0 || c < 0 || a >= n_pts || b >= n_pts || c >= n_pts) {
+      badid = 1;
+      continue;
+    }
+    int32_t i0, i1, i2;
+    float nx, ny, nz;
+    face_normal(p, conn, t, &i0, &i1, &i2, &nx, &ny, &nz);
+    m = fmaxf(m, fmaxf(fabsf(nx), fmaxf(fabsf(ny), fabsf(nz))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    badid |= __shfl_xor_sync(0xffffffffu, badid, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    if (m > 0.f) atomicMax(maxbits, __float_as_uint(m));  // NaN/inf never win a max here
+    if (badid) atomicOr(bad, 1u);
+  }
+}
+
+// Power-of-two scale from the largest component (its f32 exponent).
+__device__ __forceinline__ int normals_shift(unsigned maxbits) {
+  if (maxbits == 0u || maxbits >= 0x7f800000u) return 0;  // no faces, or inf/NaN: unscaled
+  const int e = (int)((maxbits >> 23) & 0xff) - 127;       // max < 2^(e+1)
+  return 62 - kNormValence - (e + 1);                      // max * 2^shift < 2^(62-valence)
+}
+
+// Pass 2: add each face normal to its three vertices, in fixed point.
+// A face normal that is not finite makes its vertices' normals NaN, as the
+// reference's f32 sums would (nan[v] flags them).
+__global__ void __launch_bounds__(kThreads)
+k_normals_accumulate(const float* __restrict__ p, const int32_t* __restrict__ conn,
+                     int64_t n_tris, const unsigned* __restrict__ maxbits,
+                     unsigned long long* __restrict__ acc, unsigned* __restrict__ nan) {
+  const int shift = normals_shift(*maxbits);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n_tris; t += stride) {
+    int32_t i0, i1, i2;
+    float nx, ny, nz;
+    face_normal(p, conn, t, &i0, &i1, &i2, &nx, &ny, &nz);
+    if (!isfinite(nx) || !isfinite(ny) || !isfinite(nz)) {
+      nan[i0] = 1u;
+      nan[i1] = 1u;
+      nan[i2] = 1u;
+      continue;
+    }
+    const unsigned long long fx = (unsigned long long)__double2ll_rn(ldexp((double)nx, shift));
+    const unsigned long long fy = (unsigned long long)__double2ll_rn(ldexp((double)ny, shift));
+    const unsigned long long fz = (unsigned long long)__double2ll_rn(ldexp((double)nz, shift));
+    const int32_t ids[3] = {i0, i1, i2};
+#pragma unroll
+    for (int v = 0; v < 3; ++v) {
+      unsigned long long* a = acc + 3 * (int64_t)ids[v];
+      atomicAdd(a, fx);
+      atomicAdd(a + 1, fy);
+      atomicAdd(a + 2, fz);
+    }
+  }
+}
+
+// Pass 3: back to f32 and normalise where the length exceeds 1e-10
+// (compute_normals.py:63-76; a shorter vector is left as summed).
+__global__ void __launch_bounds__(kThreads)
+k_normals_normalize(const unsigned long long* __restrict__ acc, const unsigned* __restrict__ nan,
+                    int64_t n_pts, const unsigned* __restrict__ maxbits, float* __restrict__ out) {
+  const int shift = normals_shift(*maxbits);
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_pts; i += stride) {
+    if (nan[i]) {
+      out[3 * i] = out[3 * i + 1] = out[3 * i + 2] = __int_as_float(0x7fffffff);
+      continue;
+    }
+    const double x = ldexp((double)(long long)acc[3 * i], -shift);
+    const double y = ldexp((double)(long long)acc[3 * i + 1], -shift);
+    const double z = ldexp((double)(long long)acc[3 * i + 2], -shift);
+    const double len = sqrt(x * x + y * y + z * z);
+    float* o = out + 3 * i;
+    if (len > 1.0e-10) {
+      o[0] = (float)(x / len);
+      o[1] = (float)(y / len);
+      o[2] = (float)(z / len);
+    } else {
+      o[0] = (float)x;
+      o[1] = (float)y;
+      o[2] = (float)z;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
 // per-cell classification (26_marching_cubes.py:435-450)
 // ------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads)
@@ -2684,6 +2816,46 @@ int tkmc_mc_tables(int32_t* tri_table, int32_t* num_tris, int32_t* edge_corners)
 // ---- reductions ----------------------------------------------------------
 
 static int reduce_grid(int64_t n) { return grid_for((n + 3) / 4, kThreads * 8, 4); }
+
+size_t tkmc_normals_workspace_bytes(int64_t n_pts) {
+  if (n_pts < 0) return 0;
+  return 256 + align_up((size_t)n_pts * 3 * sizeof(unsigned long long), 256) +
+         align_up((size_t)n_pts * sizeof(unsigned), 256);
+}
+
+int tkmc_compute_normals(const float* points, const int32_t* conn, int64_t n_pts, int64_t n_tris,
+                         void* ws, size_t ws_bytes, float* normals, void* stream) {
+  if (n_pts < 0 || n_tris < 0) return set_err(TKMC_ERR_INVALID_ARG, "negative size");
+  if ((n_tris > 0 && (!points || !conn)) || (n_pts > 0 && !normals))
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_compute_normals: NULL argument");
+  int rc = check_ws(ws, ws_bytes, tkmc_normals_workspace_bytes(n_pts));
+  if (rc) return rc;
+  if (n_pts > INT32_MAX) return set_err(TKMC_ERR_OVERFLOW, "more than INT32_MAX points");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned* maxbits = static_cast<unsigned*>(ws);
+  unsigned* bad = maxbits + 1;
+  unsigned long long* acc = reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + 256);
+  unsigned* nan = reinterpret_cast<unsigned*>(
+      static_cast<char*>(ws) + 256 + align_up((size_t)n_pts * 3 * sizeof(unsigned long long), 256));
+  TK_CUDA(cudaMemsetAsync(ws, 0, tkmc_normals_workspace_bytes(n_pts), st));
+  if (n_tris > 0) {
+    const int g = grid_for(n_tris, kThreads, 8);
+    k_normals_max<<<g, kThreads, 0, st>>>(points, conn, n_pts, n_tris, maxbits, bad);
+    TK_LAUNCHED();
+    unsigned hbad = 0;
+    TK_CUDA(cudaMemcpyAsync(&hbad, bad, sizeof(hbad), cudaMemcpyDeviceToHost, st));
+    TK_CUDA(cudaStreamSynchronize(st));
+    if (hbad) return set_err(TKMC_ERR_INVALID_ARG, "conn holds a point id outside [0, n_pts)");
+    k_normals_accumulate<<<g, kThreads, 0, st>>>(points, conn, n_tris, maxbits, acc, nan);
+    TK_LAUNCHED();
+  }
+  if (n_pts > 0) {
+    k_normals_normalize<<<grid_for(n_pts, kThreads, 8), kThreads, 0, st>>>(acc, nan, n_pts,
+                                                                          maxbits, normals);
+    TK_LAUNCHED();
+  }
+  return TKMC_OK;
+}
 
 size_t tkmc_reduce_workspace_bytes(int64_t n) {
   if (n < 0) return 0;

@@ -17,6 +17,8 @@ What is recorded (all through the reference's public or module-level API):
                     classify_cells and their exclusive_scan offsets
   scan.npz          tack.algorithms.exclusive_scan / inclusive_scan outputs
   reduce.npz        Field.sum/min/max outputs on tack.cpu
+  normals.npz       tack.algorithms.compute_normals on small meshes, a random
+                    mesh and a flying-edges sphere (compute_normals.py:16-90)
 """
 
 import argparse
@@ -278,6 +280,56 @@ def run_reduce(tack, out_dir):
     np.savez_compressed(os.path.join(out_dir, "reduce.npz"), **rec)
 
 
+def normals_cases():
+    """Meshes for compute_normals: the kinds the reference's tests use
+    (one triangle either winding, a flat quad, two faces folded 90 degrees,
+    a big and a tiny face sharing a vertex, a vertex no face touches, a
+    zero-area face), a flying-edges sphere, and a random shared-vertex mesh."""
+    cases = {
+        "tri_ccw": (np.array([[0, 0, 0], [1, 0, 0], [0, 1, 0]]), np.array([[0, 1, 2]])),
+        "tri_cw": (np.array([[0, 0, 0], [1, 0, 0], [0, 1, 0]]), np.array([[0, 2, 1]])),
+        "quad": (np.array([[0, 0, 0], [2, 0, 0], [2, 3, 0], [0, 3, 0]]),
+                 np.array([[0, 1, 2], [0, 2, 3]])),
+        "fold": (np.array([[0, 0, 0], [1, 0, 0], [1, 1, 0], [0, 1, 0], [0, 0, 1], [0, 1, 1]]),
+                 np.array([[0, 1, 2], [0, 2, 3], [0, 5, 3], [0, 4, 5]])),
+        "big_small": (np.array([[0, 0, 0], [8, 0, 0], [0, 8, 0], [0, 0, 0.02], [0, 0.02, 0]]),
+                      np.array([[0, 1, 2], [0, 3, 4]])),
+        "unreferenced": (np.array([[0, 0, 0], [1, 0, 0], [0, 1, 0], [4, 4, 4]]),
+                         np.array([[0, 1, 2]])),
+        "degenerate": (np.array([[0, 0, 0], [1, 0, 0], [3, 0, 0]]), np.array([[0, 1, 2]])),
+    }
+    rng = np.random.default_rng(41)
+    pts = rng.standard_normal((2000, 3))
+    tris = np.stack([rng.permutation(2000)[:3] for _ in range(6000)])
+    cases["random"] = (pts, tris)
+    return {k: (np.asarray(p, np.float32), np.asarray(c, np.int32)) for k, (p, c) in cases.items()}
+
+
+def run_normals(tack, out_dir):
+    """compute_normals on each mesh (tack.algorithms.compute_normals), and on
+    the flying-edges surface of fe_sphere24_in's volume."""
+    cn = importlib.import_module("tack.algorithms.compute_normals")
+    fe_mod = importlib.import_module("tack.algorithms.flying_edges")
+    meshes = normals_cases()
+    g = cube_grid(24)
+    v = sphere_values(g)
+    f = tack.field(dtype=tack.f32, shape=(v.size,))
+    f.from_numpy(v)
+    r = fe_mod.flying_edges(f, fe_mod.UniformGrid(*g), 0.0)
+    meshes["fe_sphere24"] = (r["points"].astype(np.float32), r["conn"].astype(np.int32))
+    rec = {}
+    for k, (p, c) in meshes.items():
+        pf = tack.field(dtype=tack.f32, shape=(p.size,))
+        pf.from_numpy(p.reshape(-1))
+        cf = tack.field(dtype=tack.i32, shape=(c.size,))
+        cf.from_numpy(c.reshape(-1))
+        out = cn.compute_normals(pf, cf, p.shape[0], c.shape[0])
+        rec[f"{k}_points"] = p
+        rec[f"{k}_conn"] = c
+        rec[f"{k}_normals"] = out.to_numpy().reshape(-1, 3)
+    np.savez_compressed(os.path.join(out_dir, "normals.npz"), **rec)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -296,6 +348,7 @@ def main():
     run_mc_classify(tack, a.reference, a.out)
     run_scan(tack, a.out)
     run_reduce(tack, a.out)
+    run_normals(tack, a.out)
     with open(os.path.join(a.out, "MANIFEST.txt"), "w") as fh:
         fh.write("Generated by tests/golden/make_golden.py from the reference on tack.cpu.\n")
         fh.write("\n".join(manifest) + "\n")

@@ -90,3 +90,15 @@ def test_oracle_thread_count_does_not_change_output(oracle):
     b = oracle.flying_edges(c["values"], g, c["isovalue"], nthreads=7)
     np.testing.assert_array_equal(a["conn"], b["conn"])
     np.testing.assert_array_equal(a["points"], b["points"])
+
+
+def test_oracle_normals_match_reference(oracle):
+    """compute_normals.py:16-90 restated: the reference's normals on every
+    fixture mesh (small meshes of its tests' kinds, a random mesh, a
+    flying-edges sphere), bit for bit."""
+    z = np.load(f"{GOLDEN}/normals.npz")
+    names = sorted({k.rsplit("_", 1)[0] for k in z.files})
+    assert len(names) >= 9
+    for n in names:
+        got = oracle.compute_normals(z[f"{n}_points"], z[f"{n}_conn"])
+        np.testing.assert_array_equal(got.view(np.uint32), z[f"{n}_normals"].view(np.uint32), n)
