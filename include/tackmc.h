@@ -206,6 +206,32 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
                         const void* workspace, size_t workspace_bytes,
                         int64_t* dst, void* stream);
 
+/* Unmerged triangle soup of the last tkmc_fe_count on this workspace (a
+ * single volume, ghost_plane 0): the same triangles in the same order as
+ * tkmc_fe_emit's conn, every vertex written out, SoA: out_x/out_y/out_z
+ * [3*T] with vertex v of triangle t at 3t+v, positions computed as
+ * 26_marching_cubes.py:453-503 (emit_triangles) computes them (cell bounds
+ * x_lo = x0 + float(i)*dx, x_hi = x_lo + dx, corner x_lo + cx*(x_hi -
+ * x_lo)).  tri_out_base[q] = first triangle row of isovalue q.
+ * tri_capacity = triangles the arrays hold; writes beyond are skipped and
+ * reported by tkmc_fe_check.  Asynchronous.  No counterpart in the
+ * reference library: example 26's classify_cells + exclusive_scan +
+ * emit_triangles pipeline. */
+int tkmc_fe_emit_soup(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                      const float* geom6, const float* isovalues, int niso,
+                      const int32_t* mask, void* workspace, size_t workspace_bytes,
+                      const int64_t* tri_out_base, float* out_x, float* out_y,
+                      float* out_z, int64_t tri_capacity, void* stream);
+
+/* Copy the device status word of each isovalue (niso int64: 0, or the
+ * TKMC_ERR_* code the last count/emit recorded -- TKMC_ERR_DEVICE_TIMEOUT,
+ * TKMC_ERR_CAPACITY) to dst (device or page-locked host memory), so that
+ * the status of many workspaces can be read with one synchronisation.
+ * Asynchronous. */
+int tkmc_fe_copy_status(int64_t nx, int64_t ny, int64_t nz, int niso,
+                        const void* workspace, size_t workspace_bytes,
+                        int64_t* dst, void* stream);
+
 /* Device-side planning: from DEVICE all_counts_dev[world][niso][4] (the
  * totals of every z-slab part, in z order; for one volume world = 1 and the
  * workspace's own totals) write bases_dev[niso*7] for part `rank`: point ids

@@ -378,6 +378,68 @@ void orc_mc_classify_cells(const float* s, const orc_grid* g, const int32_t* num
   parallel_for(g->nx * g->ny * g->nz, nthreads, classify_range, &c);
 }
 
+/* ---- emit_triangles of examples/26_marching_cubes.py:453-503 ----------- */
+/* The unmerged triangle soup: per cell, in cell order, the tri-table's
+ * vertices interpolated between the edge's two corners, corner positions
+ * from the cell's bounds (x_lo = x0 + float(ci)*dx, x_hi = x_lo + dx, corner
+ * x = x_lo + cx * (x_hi - x_lo)), SoA out. */
+static const float kCornerX[8] = {0, 1, 1, 0, 0, 1, 1, 0};
+static const float kCornerY[8] = {0, 0, 1, 1, 0, 0, 1, 1};
+static const float kCornerZ[8] = {0, 0, 0, 0, 1, 1, 1, 1};
+
+typedef struct {
+  const float* s;
+  const orc_grid* g;
+  const int32_t* tri_table;
+  const int32_t* edge_corners;
+  float iso;
+  const int64_t* offsets;
+  float *ox, *oy, *oz;
+} soup_ctx;
+
+static void soup_range(void* p, int64_t lo, int64_t hi) {
+  const soup_ctx* c = (const soup_ctx*)p;
+  const orc_grid* g = c->g;
+  const int64_t nx_p1 = g->nx + 1, nxy_p1 = nx_p1 * (g->ny + 1), nxy = g->nx * g->ny;
+  for (int64_t cell = lo; cell < hi; ++cell) {
+    const int64_t ci = cell % g->nx, cj = (cell / g->nx) % g->ny, ck = cell / nxy;
+    const int64_t b = ck * nxy_p1 + cj * nx_p1 + ci;
+    const int64_t pt[8] = {b, b + 1, b + nx_p1 + 1, b + nx_p1,
+                           b + nxy_p1, b + nxy_p1 + 1, b + nxy_p1 + nx_p1 + 1, b + nxy_p1 + nx_p1};
+    float v[8];
+    int case_idx = 0;
+    for (int q = 0; q < 8; ++q) {
+      v[q] = c->s[pt[q]];
+      if (v[q] > c->iso) case_idx += 1 << q;
+    }
+    const float x_lo = g->x0 + (float)ci * g->dx, x_hi = x_lo + g->dx;
+    const float y_lo = g->y0 + (float)cj * g->dy, y_hi = y_lo + g->dy;
+    const float z_lo = g->z0 + (float)ck * g->dz, z_hi = z_lo + g->dz;
+    int64_t out = c->offsets[cell] * 3;
+    for (int t = 0; t < 16; ++t) {
+      const int e = c->tri_table[case_idx * 16 + t];
+      if (e < 0) continue;
+      const int ca = c->edge_corners[2 * e], cb = c->edge_corners[2 * e + 1];
+      const float va = v[ca], vb = v[cb];
+      const float interp = (c->iso - va) / (vb - va + 1e-10f);
+      const float xa = x_lo + kCornerX[ca] * (x_hi - x_lo), xb = x_lo + kCornerX[cb] * (x_hi - x_lo);
+      const float ya = y_lo + kCornerY[ca] * (y_hi - y_lo), yb = y_lo + kCornerY[cb] * (y_hi - y_lo);
+      const float za = z_lo + kCornerZ[ca] * (z_hi - z_lo), zb = z_lo + kCornerZ[cb] * (z_hi - z_lo);
+      c->ox[out] = xa + interp * (xb - xa);
+      c->oy[out] = ya + interp * (yb - ya);
+      c->oz[out] = za + interp * (zb - za);
+      ++out;
+    }
+  }
+}
+
+void orc_mc_soup(const float* s, const orc_grid* g, const int32_t* tri_table,
+                 const int32_t* edge_corners, float iso, const int64_t* offsets, float* ox,
+                 float* oy, float* oz, int nthreads) {
+  soup_ctx c = {s, g, tri_table, edge_corners, iso, offsets, ox, oy, oz};
+  parallel_for(g->nx * g->ny * g->nz, nthreads, soup_range, &c);
+}
+
 /* ---- exclusive_scan / inclusive_scan (scan.py:81-123), serial ---------- */
 
 int64_t orc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive) {

@@ -78,6 +78,8 @@ def lib():
         L.orc_scan_i32.argtypes = [P, P, I64, I]
         L.orc_scan_i32.restype = I64
         L.orc_reduce_f32.argtypes = [P, I64, P]
+        L.orc_mc_soup.argtypes = [P, G, P, P, F, P, P, P, P, I]
+        L.orc_mc_soup.restype = None
         L.orc_compute_normals.argtypes = [P, P, I64, I64, P]
         L.orc_compute_normals.restype = None
         L.orc_num_threads.argtypes = [I]
@@ -293,3 +295,22 @@ def compute_normals(points, conn):
     out = np.zeros(3 * n_pts, np.float32)
     lib().orc_compute_normals(_ptr(p), _ptr(c), n_pts, n_tris, _ptr(out))
     return out.reshape(-1, 3)
+
+
+def mc_soup(values, grid, isovalue, nthreads=0):
+    """classify_cells + exclusive_scan + emit_triangles of
+    examples/26_marching_cubes.py:435-503: the unmerged triangle soup as
+    SoA f32 arrays (x, y, z) of 3*T vertices, and T."""
+    g = Grid.of(grid)
+    v = _f32(values, g)
+    cases, ntri = classify_cells(v, g, isovalue, nthreads)
+    off = np.zeros(ntri.size, np.int64)
+    if ntri.size:
+        off[1:] = np.cumsum(ntri[:-1], dtype=np.int64)
+    total = int(ntri.sum(dtype=np.int64))
+    out = [np.zeros(max(3 * total, 1), np.float32) for _ in range(3)]
+    tri, _, edges = tables()
+    gc = g.c()
+    lib().orc_mc_soup(_ptr(v), ctypes.byref(gc), _ptr(tri), _ptr(edges), np.float32(isovalue),
+                      _ptr(off), _ptr(out[0]), _ptr(out[1]), _ptr(out[2]), nthreads)
+    return out[0][:3 * total], out[1][:3 * total], out[2][:3 * total], total

@@ -43,6 +43,9 @@ SIGNATURES = {
     "tkmc_fe_emit_dev": (_I, [_P, _I64, _I64, _I64, _I, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P,
                               _I64, _P, _I64, _P]),
     "tkmc_fe_copy_counts": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P, _P]),
+    "tkmc_fe_copy_status": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P, _P]),
+    "tkmc_fe_emit_soup": (_I, [_P, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P,
+                               _I64, _P]),
     "tkmc_fe_plan": (_I, [_P, _I, _I, _I, _I, _P, _P]),
     "tkmc_fe_clear_capacity_error": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P]),
     "tkmc_fe_count": (_I, [_P, _I64, _I64, _I64, _I, _P, _I, _P, _P, _SZ, _P, _P]),

@@ -8,5 +8,5 @@ Mirrors the names tack exports from ``tack.algorithms`` for this path
 from .compute_normals import compute_normals  # noqa: F401
 from .flying_edges import (MCTables, UniformGrid, flying_edges,  # noqa: F401
                            flying_edges_multiblock)
-from .marching_cubes import classify_cells  # noqa: F401
+from .marching_cubes import classify_cells, marching_cubes_soup  # noqa: F401
 from .scan import exclusive_scan, inclusive_scan  # noqa: F401

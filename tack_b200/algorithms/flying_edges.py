@@ -163,6 +163,16 @@ class _Block:
         self.counts = []  # per isovalue group: (host int64 [niso*4], workspace)
 
 
+def _raise_status(status, phase):
+    """Raise for the first device status word that records an error."""
+    bad = np.nonzero(status)[0]
+    if bad.size:
+        code = int(status[bad[0]])
+        what = ("device wait expired" if code == _lib.TKMC_ERR_DEVICE_TIMEOUT else
+                "output capacity exceeded" if code == _lib.TKMC_ERR_CAPACITY else "error")
+        raise _lib.TkmcError(code, f"flying edges {phase}: {what} (status {code})")
+
+
 def flying_edges(scalar, grid, isovalue, *, copy_to_host=True):
     """Isosurface a single uniform grid block.
 
@@ -206,10 +216,16 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
     bl = [_Block(b, i) for i, b in enumerate(blocks)]
     groups = [isos[i:i + _lib.MAX_ISO] for i in range(0, len(isos), _lib.MAX_ISO)]
 
-    # Pass 1: count every (block, isovalue group).  Emit needs each part's
-    # offsets, so a call with several parts gives each its own workspace;
-    # a single part reuses this thread's cached one.
+    # Pass 1: count every (block, isovalue group) -- classify and scan are
+    # queued for all parts, their totals and status words copied to pinned
+    # host memory, and read with ONE synchronisation.  Emit needs each
+    # part's offsets, so a call with several parts gives each its own
+    # workspace; a single part reuses this thread's cached one.
     private = len(bl) * len(groups) > 1
+    nparts = len(bl) * len(groups)
+    counts_h = torch.zeros(nparts * _lib.MAX_ISO * 4, dtype=torch.int64, pin_memory=True)
+    status_h = torch.zeros(nparts * _lib.MAX_ISO, dtype=torch.int64, pin_memory=True)
+    part = 0
     for b in bl:
         g = b.grid
         for grp in groups:
@@ -218,12 +234,23 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
                 raise ValueError(f"unsupported grid {g.nx} x {g.ny} x {g.nz}")
             ws = (torch.empty(nbytes, dtype=torch.uint8, device=dev) if private
                   else workspace("fe", nbytes, dev))
-            counts = np.zeros(4 * len(grp), np.int64)
-            _lib.check(lib.tkmc_fe_count(
-                b.scalar.data_ptr(), g.nx, g.ny, g.nz, 0, _f32_array(grp), len(grp),
-                b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(), ws.numel(),
-                counts.ctypes.data, stream), "tkmc_fe_count")
-            b.counts.append((counts, ws))
+            mptr = b.mask.data_ptr() if b.mask is not None else None
+            isoc = _f32_array(grp)
+            _lib.check(lib.tkmc_fe_classify(b.scalar.data_ptr(), g.nx, g.ny, g.nz, isoc, len(grp),
+                                            ws.data_ptr(), ws.numel(), stream), "tkmc_fe_classify")
+            _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, g.nz, 0, len(grp), mptr, ws.data_ptr(),
+                                        ws.numel(), stream), "tkmc_fe_scan")
+            base = part * _lib.MAX_ISO
+            _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(),
+                                               ws.numel(), counts_h.data_ptr() + 8 * 4 * base,
+                                               stream), "tkmc_fe_copy_counts")
+            _lib.check(lib.tkmc_fe_copy_status(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(),
+                                               ws.numel(), status_h.data_ptr() + 8 * base,
+                                               stream), "tkmc_fe_copy_status")
+            b.counts.append((counts_h.numpy()[4 * base:4 * (base + len(grp))], ws))
+            part += 1
+    torch.cuda.current_stream(dev).synchronize()
+    _raise_status(status_h.numpy(), "count")
 
     # Layout: isovalue-major, then block, then the X | Y | Z sections.
     niso, nblk = len(isos), len(bl)
@@ -266,14 +293,21 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
                 len(grp), b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(),
                 ws.numel(), ida, ida, _i64_array(tri_base), points_t.data_ptr(), total_points,
                 conn_t.data_ptr(), total_tris, stream), "tkmc_fe_emit")
-    # Surface any error the kernels recorded (bounded waits, capacity).
+    # Surface any error the kernels recorded (capacity), one synchronisation
+    # for all parts.
+    part = 0
     for b in bl:
         g = b.grid
         for gi, grp in enumerate(groups):
             _, ws = b.counts[gi]
-            _lib.check(lib.tkmc_fe_check(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(), ws.numel(),
-                                         stream), "tkmc_fe_check")
+            _lib.check(lib.tkmc_fe_copy_status(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(),
+                                               ws.numel(),
+                                               status_h.data_ptr() + 8 * part * _lib.MAX_ISO,
+                                               stream), "tkmc_fe_copy_status")
+            part += 1
 
+    if not copy_to_host:
+        torch.cuda.current_stream(dev).synchronize()
     points_field = Field(f32, (total_points * 3,), CUDABuffer(points_t))
     conn_field = Field(i32, (total_tris * 3,), CUDABuffer(conn_t))
     points_h = conn_h = None
@@ -285,6 +319,7 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
         points_h.copy_(points_t, non_blocking=True)
         conn_h.copy_(conn_t, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
+    _raise_status(status_h.numpy(), "emit")
     out = {
         "points": points_h.numpy().reshape(-1, 3) if copy_to_host else None,
         "conn": conn_h.numpy().reshape(-1, 3) if copy_to_host else None,

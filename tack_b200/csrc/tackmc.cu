@@ -2255,6 +2255,121 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
 }
 
 // ------------------------------------------------------------------------
+// unmerged triangle soup (26_marching_cubes.py:453-503)
+// ------------------------------------------------------------------------
+//
+// The same triangles as the merged output, in the same order (cell order,
+// tri-table order), but every vertex written out on its own, SoA x/y/z, with
+// example 26's arithmetic: the cell's bounds x_lo = x0 + float(i)*dx,
+// x_hi = x_lo + dx, an edge's corners at x_lo + cx*(x_hi - x_lo), and the
+// vertex xa + t*(xb - xa), t = (iso - va)/((vb - va) + 1e-10).  One warp per
+// cell row: its triangle offset from the row table, its words with output
+// from the row's activity mask, lane = cell within a word, a warp prefix of
+// the cells' triangle counts for their slots.
+__constant__ int c_edge_corners[24] = {0, 1, 1, 2, 3, 2, 0, 3, 4, 5, 5, 6,
+                                       7, 6, 4, 7, 0, 4, 1, 5, 3, 7, 2, 6};
+__constant__ float c_corner_xyz[3][8] = {{0, 1, 1, 0, 0, 1, 1, 0},
+                                         {0, 0, 1, 1, 0, 0, 1, 1},
+                                         {0, 0, 0, 0, 1, 1, 1, 1}};
+
+__global__ void __launch_bounds__(kThreads)
+k_fe_emit_soup(FeDims d, FeWsAll ws, FeEmitArgs A, float* __restrict__ ox,
+               float* __restrict__ oy, float* __restrict__ oz) {
+  __shared__ uint64_t s_case[256];
+  const int isoi = blockIdx.y;
+  const FeIsoWs& W = ws.iso[isoi];
+  const int tid = threadIdx.x, lane = tid & 31;
+  s_case[tid] = c_case_tris[tid];  // kThreads == 256
+  __syncthreads();
+  const int64_t L = d.L, plane = d.L * d.M;
+  const float iso = A.iso.v[isoi];
+  const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
+  const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
+  const long long tri0 = base_tri(A, isoi);
+  const int64_t ncrows = d.ny * (d.N - 1);  // cell rows of this slab
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t cr = gw; cr < ncrows; cr += nw) {
+    const int64_t j = cr % d.ny, k = cr / d.ny;
+    const int64_t r = k * d.M + j;
+    const long long t_begin = __ldcg(W.rowoff + r * 4 + 3);
+    if (__ldcg(W.rowoff + (r + 1) * 4 + 3) == t_begin) continue;  // no triangles
+    long long tb = tri0 + t_begin;
+    const float y_lo = __fadd_rn(y0, __fmul_rn(__ll2float_rn((long long)j), hy));
+    const float y_hi = __fadd_rn(y_lo, hy);
+    const float z_lo = __fadd_rn(z0, __fmul_rn(__ll2float_rn((long long)(k + A.k_offset)), hz));
+    const float z_hi = __fadd_rn(z_lo, hz);
+    const int64_t rowbit = r * L;
+    for (int g = 0; g < d.AW; ++g) {
+      uint32_t act = __ldcg(W.wact + r * d.AW + g);
+      while (act) {
+        const int w = 32 * g + __ffs(act) - 1;
+        act &= act - 1u;
+        uint32_t an, bn, cn, dn;
+        const uint32_t a = row_word_next(W.bits, rowbit, w, L, &an);
+        const uint32_t b = row_word_next(W.bits, rowbit + L, w, L, &bn);
+        const uint32_t c = row_word_next(W.bits, rowbit + plane, w, L, &cn);
+        const uint32_t dd = row_word_next(W.bits, rowbit + plane + L, w, L, &dn);
+        const uint32_t a1 = (a >> 1) | (an << 31), b1 = (b >> 1) | (bn << 31);
+        const uint32_t c1 = (c >> 1) | (cn << 31), d1 = (dd >> 1) | (dn << 31);
+        const int64_t i = 32 * (int64_t)w + lane;
+        uint64_t pkc = 0;
+        unsigned nt = 0;
+        if (i < d.nx && !(A.mask && __ldg(A.mask + (k * d.ny + j) * d.nx + i) != 0)) {
+          pkc = s_case[cell_case(lane, a, a1, b, b1, c, c1, dd, d1)];
+          nt = (unsigned)(pkc >> 60);
+        }
+        unsigned ex = nt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const unsigned y = __shfl_up_sync(0xffffffffu, ex, o);
+          if (lane >= o) ex += y;
+        }
+        const unsigned total = __shfl_sync(0xffffffffu, ex, 31);
+        ex -= nt;
+        if (nt) {
+          const long long t0 = tb + ex;
+          if (t0 < 0 || t0 + nt > A.conn_cap) {
+            record_overflow(W.info);
+          } else {
+            const int64_t n0 = rowbit + i;
+            float v[8];
+            v[0] = __ldg(A.v + n0);
+            v[1] = __ldg(A.v + n0 + 1);
+            v[2] = __ldg(A.v + n0 + L + 1);
+            v[3] = __ldg(A.v + n0 + L);
+            v[4] = __ldg(A.v + n0 + plane);
+            v[5] = __ldg(A.v + n0 + plane + 1);
+            v[6] = __ldg(A.v + n0 + plane + L + 1);
+            v[7] = __ldg(A.v + n0 + plane + L);
+            const float x_lo = __fadd_rn(x0, __fmul_rn(__ll2float_rn((long long)i), hx));
+            const float x_hi = __fadd_rn(x_lo, hx);
+            const float lo[3] = {x_lo, y_lo, z_lo};
+            const float wd[3] = {__fsub_rn(x_hi, x_lo), __fsub_rn(y_hi, y_lo),
+                                 __fsub_rn(z_hi, z_lo)};
+            float* outs[3] = {ox, oy, oz};
+            for (unsigned q = 0; q < 3 * nt; ++q) {
+              const int e = (int)((pkc >> (4 * q)) & 0xfu);
+              const int ca = c_edge_corners[2 * e], cb = c_edge_corners[2 * e + 1];
+              const float va = v[ca], vb = v[cb];
+              const float tt = __fdiv_rn(__fsub_rn(iso, va), __fadd_rn(__fsub_rn(vb, va), 1.0e-10f));
+              const int64_t slot = (t0 + q / 3) * 3 + q % 3;
+#pragma unroll
+              for (int ax = 0; ax < 3; ++ax) {
+                const float pa = __fadd_rn(lo[ax], __fmul_rn(c_corner_xyz[ax][ca], wd[ax]));
+                const float pb = __fadd_rn(lo[ax], __fmul_rn(c_corner_xyz[ax][cb], wd[ax]));
+                outs[ax][slot] = __fadd_rn(pa, __fmul_rn(tt, __fsub_rn(pb, pa)));
+              }
+            }
+          }
+        }
+        tb += total;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------
 // device-side planning: output bases without a host round trip
 // ------------------------------------------------------------------------
 //
@@ -3210,6 +3325,56 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso, const void
                             static_cast<const char*>(ws) + f.off_info, 16 * sizeof(long long),
                             4 * sizeof(long long), (size_t)niso, cudaMemcpyDefault,
                             static_cast<cudaStream_t>(stream)));
+  return TKMC_OK;
+}
+
+int tkmc_fe_emit_soup(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
+                      const float* geom6, const float* isovalues, int niso, const int32_t* mask,
+                      void* ws, size_t ws_bytes, const int64_t* tri_out_base, float* out_x,
+                      float* out_y, float* out_z, int64_t tri_capacity, void* stream) {
+  int rc = check_iso(isovalues, niso);
+  if (rc) return rc;
+  FeLayout f;
+  if (!fe_layout(nx, ny, nz, 0, niso, &f)) return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  if ((rc = check_ws(ws, ws_bytes, f.total))) return rc;
+  if (!scalar || !geom6 || !tri_out_base || (tri_capacity > 0 && (!out_x || !out_y || !out_z)))
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_emit_soup: NULL argument");
+  FeEmitArgs A{};
+  A.v = scalar;
+  A.mask = mask;
+  A.conn_cap = tri_capacity;
+  for (int i = 0; i < 6; ++i) A.geom[i] = geom6[i];
+  for (int q = 0; q < niso; ++q) {
+    A.iso.v[q] = isovalues[q];
+    A.tri_out_base[q] = tri_out_base[q];
+  }
+  FeWsAll v = fe_views(f, ws, niso);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((f.d.L & 31) == 0) {  // word-aligned rows keep offsets per unit: fill the row table
+    k_fe_offsets_units<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
+        f.d, v, f.unit_cap, 1);
+    TK_LAUNCHED();
+  }
+  const int64_t ncrows = ny * nz;
+  if (ncrows > 0 && nx > 0) {
+    k_fe_emit_soup<<<dim3((unsigned)grid_for(ncrows, kThreads / 32, 8), (unsigned)niso), kThreads, 0,
+                     st>>>(f.d, v, A, out_x, out_y, out_z);
+    TK_LAUNCHED();
+  }
+  return TKMC_OK;
+}
+
+int tkmc_fe_copy_status(int64_t nx, int64_t ny, int64_t nz, int niso, const void* ws,
+                        size_t ws_bytes, int64_t* dst, void* stream) {
+  FeLayout f;
+  if (!fe_layout(nx, ny, nz, 0, niso, &f)) return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  int rc = check_ws(const_cast<void*>(ws), ws_bytes, f.total);
+  if (rc) return rc;
+  if (!dst) return set_err(TKMC_ERR_INVALID_ARG, "dst is NULL");
+  TK_CUDA(cudaMemcpy2DAsync(dst, sizeof(long long),
+                            static_cast<const char*>(ws) + f.off_info + 10 * sizeof(long long),
+                            16 * sizeof(long long), sizeof(long long), (size_t)niso,
+                            cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
   return TKMC_OK;
 }
 

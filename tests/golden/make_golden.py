@@ -14,7 +14,8 @@ What is recorded (all through the reference's public or module-level API):
                     flying_edges result (points, conn, totals) and its
                     _count_block row counts and offsets (flying_edges.py:663-715)
   mc_classify.npz   per-cell triangle counts from examples/26_marching_cubes.py
-                    classify_cells and their exclusive_scan offsets
+                    classify_cells, their exclusive_scan offsets, and the
+                    unmerged triangle soup of its emit_triangles
   scan.npz          tack.algorithms.exclusive_scan / inclusive_scan outputs
   reduce.npz        Field.sum/min/max outputs on tack.cpu
   normals.npz       tack.algorithms.compute_normals on small meshes, a random
@@ -219,7 +220,9 @@ def run_mc_classify(tack, root, out_dir):
     rec = {}
     for name, values, g, iso in (("c1", sphere_sdf64(), (63, 63, 63, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0), 0.0),
                                  ("noise", noise_values((19, 13, 11), 16, 0.1, 0.02, 0.05),
-                                  (19, 13, 11, 0.5, -0.25, 1.0, 0.75, 1.25, 0.5), 0.1)):
+                                  (19, 13, 11, 0.5, -0.25, 1.0, 0.75, 1.25, 0.5), 0.1),
+                                 ("aligned", noise_values((63, 9, 5), 23, -0.2, 0.01, 0.02),
+                                  (63, 9, 5, -3.0, 2.0, 0.125, 0.3, 0.7, 1.1), -0.2)):
         grid = ex["UniformGrid3D"](*g)
         tables = ex["MCTables"]()
         n_cells = g[0] * g[1] * g[2]
@@ -235,6 +238,11 @@ def run_mc_classify(tack, root, out_dir):
         rec[f"{name}_num_tri"] = num_tri.to_numpy()
         rec[f"{name}_offsets"] = offsets.to_numpy()
         rec[f"{name}_total"] = np.int64(total)
+        # The unmerged triangle soup of emit_triangles (SoA x, y, z).
+        outs = [tack.field(dtype=tack.f32, shape=(max(3 * total, 1),)) for _ in range(3)]
+        ex["emit_triangles"](f, offsets, grid, tables, *outs, n_cells, iso)
+        for axis, o in zip("xyz", outs):
+            rec[f"{name}_soup_{axis}"] = o.to_numpy()[:3 * total]
     np.savez_compressed(os.path.join(out_dir, "mc_classify.npz"), **rec)
 
 

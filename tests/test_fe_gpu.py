@@ -272,3 +272,33 @@ def test_volume_sizes_match_oracle(tack, oracle, shape):
         assert got["total_points"] == 0 or got["total_tris"] == 0
     else:
         assert_same_surface(got, ref)
+
+
+def test_many_blocks_match_oracle(tack, oracle):
+    """Many blocks of different shapes (word-aligned rows and not), some
+    masked, some empty: counts of all blocks are read with one
+    synchronisation, then every block emits; the concatenation equals the
+    oracle's flying_edges_multiblock."""
+    rng = np.random.default_rng(11)
+    blocks_gpu, blocks_ref = [], []
+    for b in range(40):
+        nx, ny, nz = (31 if b % 3 else 20), int(rng.integers(2, 12)), int(rng.integers(1, 9))
+        n = (nx + 1) * (ny + 1) * (nz + 1)
+        v = (rng.standard_normal(n) + (5.0 if b % 7 == 0 else 0.0)).astype(np.float32)  # some empty
+        g = (nx, ny, nz, float(b), 0.0, 0.0, 0.5, 0.5, 0.5)
+        mask = None
+        if b % 4 == 1:
+            mask = (rng.random(nx * ny * nz) < 0.3).astype(np.int32)
+        blk = {"scalar": _upload(tack, v, tack.f32), "grid": tack.UniformGrid(*g)}
+        ref = {"values": v, "grid": oracle.Grid(*g)}
+        if mask is not None:
+            blk["mask"] = _upload(tack, mask, tack.i32)
+            ref["mask"] = mask
+        blocks_gpu.append(blk)
+        blocks_ref.append(ref)
+    r = tack.flying_edges_multiblock(blocks_gpu, 0.2)
+    ref = oracle.flying_edges_multiblock(blocks_ref, 0.2)
+    np.testing.assert_array_equal(r["conn"], ref["conn"])
+    assert_points_identical(r["points"], ref["points"])
+    assert r["block_point_counts"] == list(ref["block_point_counts"])
+    assert r["block_tri_counts"] == list(ref["block_tri_counts"])

@@ -116,3 +116,54 @@ def test_classify_cases_match_oracle(tack, oracle):
     rc, rn = oracle.classify_cells(c["values"], oracle.Grid(*g), c["isovalue"])
     np.testing.assert_array_equal(cases.to_numpy(), rc)
     np.testing.assert_array_equal(ntri.to_numpy(), rn)
+
+
+def _nan_aware_equal(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    assert a.shape == b.shape
+    na, nb = np.isnan(a), np.isnan(b)
+    np.testing.assert_array_equal(na, nb)
+    np.testing.assert_array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32))
+
+
+def test_soup_matches_reference(tack):
+    """marching_cubes_soup == example 26's emit_triangles, vertex for vertex
+    (rows of a multiple of 32 nodes and not, NaNs and ties at the isovalue)."""
+    z = np.load(f"{GOLDEN}/mc_classify.npz")
+    for name in ("c1", "noise", "aligned"):
+        g = z[f"{name}_grid"]
+        grid = tack.UniformGrid(int(g[0]), int(g[1]), int(g[2]), *g[3:])
+        f = _field(tack, z[f"{name}_values"], tack.f32)
+        r = tack.algorithms.marching_cubes_soup(f, grid, float(z[f"{name}_iso"]))
+        assert r["total_tris"] == int(z[f"{name}_total"])
+        for ax in "xyz":
+            _nan_aware_equal(r[ax], z[f"{name}_soup_{ax}"])
+
+
+@pytest.mark.parametrize("shape", [(95, 60, 41), (100, 37, 30), (2047, 4, 3)])
+def test_soup_matches_oracle(tack, oracle, shape):
+    """Larger grids, several isovalues and a mask, against the oracle's
+    restatement of example 26."""
+    nx, ny, nz = shape
+    rng = np.random.default_rng(nx)
+    zz, yy, xx = np.meshgrid(np.arange(nz + 1), np.arange(ny + 1), np.arange(nx + 1), indexing="ij")
+    v = (np.sin(xx * 0.11) + np.cos(yy * 0.23) * np.sin(zz * 0.19)
+         + 0.1 * rng.standard_normal(xx.shape)).astype(np.float32).reshape(-1)
+    g = (nx, ny, nz, 0.25, -1.0, 2.0, 0.5, 0.3, 0.7)
+    isos = [0.0, 0.6]
+    r = tack.algorithms.marching_cubes_soup(_field(tack, v, tack.f32), tack.UniformGrid(*g), isos)
+    for q, iso in enumerate(isos):
+        x, y, zc, total = oracle.mc_soup(v, oracle.Grid(*g), iso)
+        assert r["isovalue_tri_counts"][q] == total
+        lo = 3 * sum(r["isovalue_tri_counts"][:q])
+        for ax, ref in zip("xyz", (x, y, zc)):
+            _nan_aware_equal(r[ax][lo:lo + 3 * total], ref)
+    mask = (rng.random(nx * ny * nz) < 0.5).astype(np.int32)
+    rm = tack.algorithms.marching_cubes_soup(_field(tack, v, tack.f32), tack.UniformGrid(*g), 0.0,
+                                             mask=_field(tack, mask, tack.i32))
+    x, y, zc, total = oracle.mc_soup(v, oracle.Grid(*g), 0.0)
+    _, ntri = oracle.classify_cells(v, oracle.Grid(*g), 0.0)
+    keep = np.repeat(mask == 0, 3 * ntri)  # the soup without the masked cells' triangles
+    assert rm["total_tris"] == int(ntri[mask == 0].sum())
+    _nan_aware_equal(rm["x"], x[keep])

@@ -41,9 +41,10 @@ def test_oracle_multiblock_matches_reference(oracle):
     assert r["block_tri_counts"] == list(z["block_tri_counts"])
 
 
-@pytest.mark.parametrize("name", ["c1", "noise"])
+@pytest.mark.parametrize("name", ["c1", "noise", "aligned"])
 def test_oracle_per_cell_counts_and_offsets(oracle, name):
-    """classify_cells + exclusive_scan of examples/26_marching_cubes.py."""
+    """classify_cells + exclusive_scan of examples/26_marching_cubes.py, and
+    its emit_triangles soup bit for bit."""
     z = np.load(f"{GOLDEN}/mc_classify.npz")
     g = z[f"{name}_grid"]
     grid = oracle.Grid(int(g[0]), int(g[1]), int(g[2]), *g[3:])
@@ -54,6 +55,10 @@ def test_oracle_per_cell_counts_and_offsets(oracle, name):
     assert total == int(z[f"{name}_total"])
     # case index -> count through the reference's table
     np.testing.assert_array_equal(oracle.tables()[1][cases], ntri)
+    x, y, zc, t = oracle.mc_soup(z[f"{name}_values"], grid, float(z[f"{name}_iso"]))
+    assert t == int(z[f"{name}_total"])
+    for got, ax in ((x, "x"), (y, "y"), (zc, "z")):
+        np.testing.assert_array_equal(got.view(np.uint32), z[f"{name}_soup_{ax}"].view(np.uint32))
 
 
 def test_oracle_scan_known_answers(oracle):
