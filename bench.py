@@ -339,10 +339,11 @@ def main():
     total_tris = int(bases["totals"][:, 1].sum())
 
     # ---- next filter on the same surface: vertex normals (one GPU) --------
-    normals = None
+    normals = soup = None
     if world == 1 and own_p > 0 and own_t > 0:
         normals = time_normals(tack, torch, pts_buf[:own_p * 3], conn_buf[:own_t * 3], own_p,
                                own_t, stream)
+        soup = time_soup(tack, torch, vol, grid, isos, cells, stream)
 
     # ---- e2e through the public API, host buffers -------------------------
     e2e = None
@@ -407,6 +408,7 @@ def main():
                            "totals_gather_plan": host, "k3_emit": k3},
             "outputs": {"points": total_points, "triangles": total_tris},
             "compute_normals": normals,
+            "marching_cubes_soup": soup,
             "gpu_launches": int(launches),
             "gpu_launches_per_step": launches / K,
             "cuda_graph": True,
@@ -438,6 +440,25 @@ def time_normals(tack, torch, points, conn, n_pts, n_tris, stream, reps=20):
     return {"ms": ms, "gtris_per_s": n_tris / (ms * 1e-3) / 1e9,
             "algorithmic_gbs": nbytes / (ms * 1e-3) / 1e9,
             "note": "deterministic 64-bit fixed-point sums; includes one host sync (id check)"}
+
+
+def time_soup(tack, torch, vol, grid, isos, cells, stream, reps=10):
+    """tack_b200.algorithms.marching_cubes_soup on the same volume (count +
+    unmerged soup + status check, device outputs): time per call (CUDA
+    events; the call synchronises twice)."""
+    iso = isos if len(isos) > 1 else isos[0]
+    for _ in range(2):
+        r = tack.algorithms.marching_cubes_soup(vol, grid, iso, copy_to_host=False)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(reps):
+        r = tack.algorithms.marching_cubes_soup(vol, grid, iso, copy_to_host=False)
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    return {"ms": ms, "gcells_per_s": cells / (ms * 1e-3) / 1e9, "triangles": r["total_tris"],
+            "output_gbs": 36.0 * r["total_tris"] / (ms * 1e-3) / 1e9}
 
 
 def ctypes_f32(vals):
