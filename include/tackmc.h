@@ -223,6 +223,42 @@ int tkmc_fe_emit_soup(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
                       const int64_t* tri_out_base, float* out_x, float* out_y,
                       float* out_z, int64_t tri_capacity, void* stream);
 
+/* ---- batches of same-shape blocks (flying_edges_multiblock) ------------ */
+/*
+ * Many blocks of one grid shape in one launch per phase instead of a
+ * sequence of launches per block (flying_edges.py:766-832 launches count
+ * and emit kernels per block, with host round trips).  vols and masks are
+ * DEVICE arrays of nblocks device pointers (masks may be NULL, or hold NULL
+ * entries); the workspace holds nblocks workspaces of
+ * tkmc_fe_batch_stride() bytes; nblocks <= 65535.
+ */
+
+/* Bytes per block of a batch workspace (a multiple of 256). */
+size_t tkmc_fe_batch_stride(int64_t nx, int64_t ny, int64_t nz, int niso);
+
+/* Count every block: counts[b*niso*4 + 4q + s] = {X, Y, Z, T} and
+ * status[b*niso + q] = the device status word (0 or TKMC_ERR_*), both
+ * copied to device or page-locked host memory (either may be NULL).
+ * Asynchronous. */
+int tkmc_fe_count_batch(const float* const* vols, int64_t nblocks, int64_t nx,
+                        int64_t ny, int64_t nz, const float* isovalues, int niso,
+                        const int32_t* const* masks, void* workspace,
+                        size_t workspace_bytes, int64_t* counts, int64_t* status,
+                        void* stream);
+
+/* Emit every block after tkmc_fe_count_batch: geoms DEVICE [nblocks][6]
+ * {x0, y0, z0, dx, dy, dz}; bases DEVICE [nblocks][niso][7] as
+ * tkmc_fe_emit_dev's (ids, output rows, triangle row of each block and
+ * isovalue); one shared output; status as in tkmc_fe_count_batch (capacity
+ * errors).  Asynchronous. */
+int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx,
+                       int64_t ny, int64_t nz, const float* geoms,
+                       const float* isovalues, int niso,
+                       const int32_t* const* masks, void* workspace,
+                       size_t workspace_bytes, const int64_t* bases,
+                       float* points, int64_t points_capacity, int32_t* conn,
+                       int64_t conn_capacity, int64_t* status, void* stream);
+
 /* Copy the device status word of each isovalue (niso int64: 0, or the
  * TKMC_ERR_* code the last count/emit recorded -- TKMC_ERR_DEVICE_TIMEOUT,
  * TKMC_ERR_CAPACITY) to dst (device or page-locked host memory), so that

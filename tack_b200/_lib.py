@@ -44,6 +44,10 @@ SIGNATURES = {
                               _I64, _P, _I64, _P]),
     "tkmc_fe_copy_counts": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P, _P]),
     "tkmc_fe_copy_status": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P, _P]),
+    "tkmc_fe_batch_stride": (_SZ, [_I64, _I64, _I64, _I]),
+    "tkmc_fe_count_batch": (_I, [_P, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _SZ, _P, _P, _P]),
+    "tkmc_fe_emit_batch": (_I, [_P, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P,
+                                _I64, _P, _I64, _P, _P]),
     "tkmc_fe_emit_soup": (_I, [_P, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P,
                                _I64, _P]),
     "tkmc_fe_plan": (_I, [_P, _I, _I, _I, _I, _P, _P]),

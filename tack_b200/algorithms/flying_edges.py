@@ -144,6 +144,7 @@ def _i64_array(vals):
 
 class _Block:
     def __init__(self, blk, idx):
+        self.idx = idx
         if "scalar" not in blk or "grid" not in blk:
             raise KeyError(f"block {idx} needs 'scalar' and 'grid'")
         self.grid = blk["grid"]
@@ -161,6 +162,87 @@ class _Block:
             raise ValueError(f"block {idx}: mask has {self.mask.numel()} values, grid has "
                              f"{g.nx * g.ny * g.nz} cells")
         self.counts = []  # per isovalue group: (host int64 [niso*4], workspace)
+
+
+class _Single:
+    """One block counted and emitted on its own."""
+
+    def __init__(self, block):
+        self.block = block
+        self.members = [block.idx]
+        self.size = 1
+        self.ws = {}
+
+    def count(self, lib, grp, gi, counts_ptr, status_ptr, stream, dev, cached_ws):
+        b, g = self.block, self.block.grid
+        nbytes = lib.tkmc_fe_workspace_bytes(g.nx, g.ny, g.nz, len(grp))
+        if nbytes == 0:
+            raise ValueError(f"unsupported grid {g.nx} x {g.ny} x {g.nz}")
+        ws = (workspace("fe", nbytes, dev) if cached_ws
+              else torch.empty(nbytes, dtype=torch.uint8, device=dev))
+        self.ws[gi] = ws
+        mptr = b.mask.data_ptr() if b.mask is not None else None
+        isoc = _f32_array(grp)
+        _lib.check(lib.tkmc_fe_classify(b.scalar.data_ptr(), g.nx, g.ny, g.nz, isoc, len(grp),
+                                        ws.data_ptr(), ws.numel(), stream), "tkmc_fe_classify")
+        _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, g.nz, 0, len(grp), mptr, ws.data_ptr(),
+                                    ws.numel(), stream), "tkmc_fe_scan")
+        _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(), ws.numel(),
+                                           counts_ptr, stream), "tkmc_fe_copy_counts")
+        _lib.check(lib.tkmc_fe_copy_status(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(), ws.numel(),
+                                           status_ptr, stream), "tkmc_fe_copy_status")
+
+    def emit(self, lib, grp, gi, bases, points_t, total_points, conn_t, total_tris, status_ptr,
+             stream, dev):
+        b, g, ws = self.block, self.block.grid, self.ws[gi]
+        ida = _i64_array(bases[0, :, 0:3].reshape(-1))
+        _lib.check(lib.tkmc_fe_emit(
+            b.scalar.data_ptr(), g.nx, g.ny, g.nz, 0, 0, _geom6(g), _f32_array(grp), len(grp),
+            b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(), ws.numel(), ida, ida,
+            _i64_array(bases[0, :, 6]), points_t.data_ptr(), total_points, conn_t.data_ptr(),
+            total_tris, stream), "tkmc_fe_emit")
+        _lib.check(lib.tkmc_fe_copy_status(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(), ws.numel(),
+                                           status_ptr, stream), "tkmc_fe_copy_status")
+
+
+class _Batch:
+    """Blocks of one grid shape: one launch per phase for all of them."""
+
+    def __init__(self, blocks, members, dev):
+        self.members = list(members)
+        self.size = len(members)
+        bs = [blocks[i] for i in members]
+        self.grid = bs[0].grid
+        self.vols = torch.tensor([b.scalar.data_ptr() for b in bs], dtype=torch.int64).to(dev)
+        has_mask = any(b.mask is not None for b in bs)
+        self.masks = (torch.tensor([b.mask.data_ptr() if b.mask is not None else 0 for b in bs],
+                                   dtype=torch.int64).to(dev) if has_mask else None)
+        self.geoms = torch.tensor([[b.grid.x0, b.grid.y0, b.grid.z0, b.grid.dx, b.grid.dy,
+                                    b.grid.dz] for b in bs], dtype=torch.float32).to(dev)
+        self.ws = {}
+
+    def count(self, lib, grp, gi, counts_ptr, status_ptr, stream, dev, cached_ws):
+        g = self.grid
+        stride = lib.tkmc_fe_batch_stride(g.nx, g.ny, g.nz, len(grp))
+        if stride == 0:
+            raise ValueError(f"unsupported grid {g.nx} x {g.ny} x {g.nz}")
+        ws = torch.empty(stride * self.size, dtype=torch.uint8, device=dev)
+        self.ws[gi] = ws
+        _lib.check(lib.tkmc_fe_count_batch(
+            self.vols.data_ptr(), self.size, g.nx, g.ny, g.nz, _f32_array(grp), len(grp),
+            self.masks.data_ptr() if self.masks is not None else None, ws.data_ptr(), ws.numel(),
+            counts_ptr, status_ptr, stream), "tkmc_fe_count_batch")
+
+    def emit(self, lib, grp, gi, bases, points_t, total_points, conn_t, total_tris, status_ptr,
+             stream, dev):
+        g, ws = self.grid, self.ws[gi]
+        bases_d = torch.from_numpy(np.ascontiguousarray(bases)).to(dev)
+        _lib.check(lib.tkmc_fe_emit_batch(
+            self.vols.data_ptr(), self.size, g.nx, g.ny, g.nz, self.geoms.data_ptr(),
+            _f32_array(grp), len(grp), self.masks.data_ptr() if self.masks is not None else None,
+            ws.data_ptr(), ws.numel(), bases_d.data_ptr(), points_t.data_ptr(), total_points,
+            conn_t.data_ptr(), total_tris, status_ptr, stream), "tkmc_fe_emit_batch")
+        self.bases_d = bases_d  # alive until the stream has used it
 
 
 def _raise_status(status, phase):
@@ -206,6 +288,10 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
         dict as flying_edges(); blocks (and isovalues) are concatenated in
         order, each block's conn offset by the points before it.  None if
         there are no points or no triangles.
+
+    Blocks that share a grid shape are counted and emitted as one batch (one
+    launch per phase for all of them); every block's totals are read with one
+    synchronisation before the output is allocated.
     """
     if len(blocks) == 0:
         return None
@@ -215,53 +301,47 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
     stream = current_stream(dev)
     bl = [_Block(b, i) for i, b in enumerate(blocks)]
     groups = [isos[i:i + _lib.MAX_ISO] for i in range(0, len(isos), _lib.MAX_ISO)]
+    niso, nblk = len(isos), len(bl)
 
-    # Pass 1: count every (block, isovalue group) -- classify and scan are
-    # queued for all parts, their totals and status words copied to pinned
-    # host memory, and read with ONE synchronisation.  Emit needs each
-    # part's offsets, so a call with several parts gives each its own
-    # workspace; a single part reuses this thread's cached one.
-    private = len(bl) * len(groups) > 1
-    nparts = len(bl) * len(groups)
-    counts_h = torch.zeros(nparts * _lib.MAX_ISO * 4, dtype=torch.int64, pin_memory=True)
-    status_h = torch.zeros(nparts * _lib.MAX_ISO, dtype=torch.int64, pin_memory=True)
-    part = 0
-    for b in bl:
-        g = b.grid
-        for grp in groups:
-            nbytes = lib.tkmc_fe_workspace_bytes(g.nx, g.ny, g.nz, len(grp))
-            if nbytes == 0:
-                raise ValueError(f"unsupported grid {g.nx} x {g.ny} x {g.nz}")
-            ws = (torch.empty(nbytes, dtype=torch.uint8, device=dev) if private
-                  else workspace("fe", nbytes, dev))
-            mptr = b.mask.data_ptr() if b.mask is not None else None
-            isoc = _f32_array(grp)
-            _lib.check(lib.tkmc_fe_classify(b.scalar.data_ptr(), g.nx, g.ny, g.nz, isoc, len(grp),
-                                            ws.data_ptr(), ws.numel(), stream), "tkmc_fe_classify")
-            _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, g.nz, 0, len(grp), mptr, ws.data_ptr(),
-                                        ws.numel(), stream), "tkmc_fe_scan")
-            base = part * _lib.MAX_ISO
-            _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(),
-                                               ws.numel(), counts_h.data_ptr() + 8 * 4 * base,
-                                               stream), "tkmc_fe_copy_counts")
-            _lib.check(lib.tkmc_fe_copy_status(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(),
-                                               ws.numel(), status_h.data_ptr() + 8 * base,
-                                               stream), "tkmc_fe_copy_status")
-            b.counts.append((counts_h.numpy()[4 * base:4 * (base + len(grp))], ws))
-            part += 1
+    # Parts: a batch of >= 2 blocks of one shape (at most 65535), or one block.
+    by_shape = {}
+    for bi, b in enumerate(bl):
+        by_shape.setdefault((b.grid.nx, b.grid.ny, b.grid.nz), []).append(bi)
+    parts = []
+    for members in by_shape.values():
+        for lo in range(0, len(members), 65535):
+            chunk = members[lo:lo + 65535]
+            parts.append(_Batch(bl, chunk, dev) if len(chunk) > 1 else _Single(bl[chunk[0]]))
+    single_ws = len(parts) == 1 and len(groups) == 1 and isinstance(parts[0], _Single)
+
+    # Pass 1: count every (part, isovalue group), totals and status words to
+    # pinned host memory, then ONE synchronisation.
+    counts_h = torch.zeros(nblk * niso * 4, dtype=torch.int64, pin_memory=True)
+    status_h = torch.zeros(2 * nblk * niso, dtype=torch.int64, pin_memory=True)
+    cnt = counts_h.numpy()
+    slot = {}  # (part index, group index) -> row offset in counts_h / status_h (in int64s)
+    row = 0
+    for pi, part in enumerate(parts):
+        for gi, grp in enumerate(groups):
+            slot[(pi, gi)] = row
+            part.count(lib, grp, gi, counts_h.data_ptr() + 8 * 4 * row,
+                       status_h.data_ptr() + 8 * row, stream, dev, single_ws)
+            row += part.size * len(grp)
     torch.cuda.current_stream(dev).synchronize()
-    _raise_status(status_h.numpy(), "count")
+    _raise_status(status_h.numpy()[:nblk * niso], "count")
 
     # Layout: isovalue-major, then block, then the X | Y | Z sections.
-    niso, nblk = len(isos), len(bl)
     pts = np.zeros((niso, nblk, 3), np.int64)
     tris = np.zeros((niso, nblk), np.int64)
-    for bi, b in enumerate(bl):
-        for gi, (counts, _) in enumerate(b.counts):
-            for q in range(len(groups[gi])):
-                qi = gi * _lib.MAX_ISO + q
-                pts[qi, bi] = counts[4 * q:4 * q + 3]
-                tris[qi, bi] = counts[4 * q + 3]
+    for pi, part in enumerate(parts):
+        for gi, grp in enumerate(groups):
+            c = cnt[4 * slot[(pi, gi)]:4 * (slot[(pi, gi)] + part.size * len(grp))]
+            c = c.reshape(part.size, len(grp), 4)
+            for k, bi in enumerate(part.members):
+                for q in range(len(grp)):
+                    qi = gi * _lib.MAX_ISO + q
+                    pts[qi, bi] = c[k, q, :3]
+                    tris[qi, bi] = c[k, q, 3]
     block_pts = pts.sum(axis=2)  # [iso, block]
     total_points = int(block_pts.sum())
     total_tris = int(tris.sum())
@@ -275,36 +355,22 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
     points_t = torch.empty(total_points * 3, dtype=torch.float32, device=dev)
     conn_t = torch.empty(total_tris * 3, dtype=torch.int32, device=dev)
 
-    # Pass 2: emit.
-    for bi, b in enumerate(bl):
-        g = b.grid
+    # Pass 2: emit every (part, isovalue group); status words after it.
+    status_e = status_h.data_ptr() + 8 * nblk * niso
+    row = 0
+    for pi, part in enumerate(parts):
         for gi, grp in enumerate(groups):
-            _, ws = b.counts[gi]
-            ids, tri_base = [], []
-            for q in range(len(grp)):
-                qi = gi * _lib.MAX_ISO + q
-                p0 = start_pt[qi, bi]
-                X, Y = pts[qi, bi, 0], pts[qi, bi, 1]
-                ids += [p0, p0 + X, p0 + X + Y]
-                tri_base.append(start_tri[qi, bi])
-            ida = _i64_array(ids)
-            _lib.check(lib.tkmc_fe_emit(
-                b.scalar.data_ptr(), g.nx, g.ny, g.nz, 0, 0, _geom6(g), _f32_array(grp),
-                len(grp), b.mask.data_ptr() if b.mask is not None else None, ws.data_ptr(),
-                ws.numel(), ida, ida, _i64_array(tri_base), points_t.data_ptr(), total_points,
-                conn_t.data_ptr(), total_tris, stream), "tkmc_fe_emit")
-    # Surface any error the kernels recorded (capacity), one synchronisation
-    # for all parts.
-    part = 0
-    for b in bl:
-        g = b.grid
-        for gi, grp in enumerate(groups):
-            _, ws = b.counts[gi]
-            _lib.check(lib.tkmc_fe_copy_status(g.nx, g.ny, g.nz, len(grp), ws.data_ptr(),
-                                               ws.numel(),
-                                               status_h.data_ptr() + 8 * part * _lib.MAX_ISO,
-                                               stream), "tkmc_fe_copy_status")
-            part += 1
+            bases = np.zeros((part.size, len(grp), 7), np.int64)
+            for k, bi in enumerate(part.members):
+                for q in range(len(grp)):
+                    qi = gi * _lib.MAX_ISO + q
+                    p0 = start_pt[qi, bi]
+                    X, Y = pts[qi, bi, 0], pts[qi, bi, 1]
+                    bases[k, q] = [p0, p0 + X, p0 + X + Y, p0, p0 + X, p0 + X + Y,
+                                   start_tri[qi, bi]]
+            part.emit(lib, grp, gi, bases, points_t, total_points, conn_t, total_tris,
+                      status_e + 8 * row, stream, dev)
+            row += part.size * len(grp)
 
     if not copy_to_host:
         torch.cuda.current_stream(dev).synchronize()
@@ -319,7 +385,7 @@ def flying_edges_multiblock(blocks, isovalue, *, copy_to_host=True):
         points_h.copy_(points_t, non_blocking=True)
         conn_h.copy_(conn_t, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
-    _raise_status(status_h.numpy(), "emit")
+    _raise_status(status_h.numpy()[nblk * niso:], "emit")
     out = {
         "points": points_h.numpy().reshape(-1, 3) if copy_to_host else None,
         "conn": conn_h.numpy().reshape(-1, 3) if copy_to_host else None,

@@ -153,6 +153,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// p moved by off bytes.
+template <typename T>
+__device__ __forceinline__ T* shift_ptr(T* p, int64_t off) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + off);
+}
+
 // Bits [0, n) set; n clamped to [0, 32].
 __device__ __forceinline__ uint32_t low_mask(int n) {
   return n >= 32 ? 0xffffffffu : (n <= 0 ? 0u : ((1u << n) - 1u));
@@ -312,7 +318,12 @@ __device__ __forceinline__ void store_summary(uint2* sums, int64_t ch, uint32_t 
 __global__ void __launch_bounds__(kThreads)
 k_fe_threshold_v4(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
                   uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
-                  uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks) {
+                  uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks,
+                  int64_t ws_stride, const float* const* vols) {
+  // A batch of same-shape blocks: blockIdx.z picks the block.
+  if (vols) v = vols[blockIdx.z];
+  bits = shift_ptr(bits, (int64_t)blockIdx.z * ws_stride);
+  sums = shift_ptr(sums, (int64_t)blockIdx.z * ws_stride);
   // nfull = chunks with all 1024 nodes present; a ragged last chunk (if
   // any) is done by k_fe_threshold_scalar.
   const int lane = threadIdx.x & 31;
@@ -357,7 +368,12 @@ k_fe_threshold_v4(const float* __restrict__ v, int64_t nfull, IsoParams iso, int
 __global__ void __launch_bounds__(kThreads, 5)
 k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
                      uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
-                     uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks) {
+                     uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks,
+                     int64_t ws_stride, const float* const* vols) {
+  // A batch of same-shape blocks: blockIdx.z picks the block.
+  if (vols) v = vols[blockIdx.z];
+  bits = shift_ptr(bits, (int64_t)blockIdx.z * ws_stride);
+  sums = shift_ptr(sums, (int64_t)blockIdx.z * ws_stride);
   const int lane = threadIdx.x & 31;
   const int64_t ch = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
@@ -391,7 +407,12 @@ k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, 
 __global__ void __launch_bounds__(kThreads)
 k_fe_threshold_scalar(const float* __restrict__ v, int64_t n, IsoParams iso, int niso,
                       uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
-                      uint2* __restrict__ sums, int64_t sums_stride, int64_t first_chunk) {
+                      uint2* __restrict__ sums, int64_t sums_stride, int64_t first_chunk,
+                      int64_t ws_stride, const float* const* vols) {
+  // A batch of same-shape blocks: blockIdx.z picks the block.
+  if (vols) v = vols[blockIdx.z];
+  bits = shift_ptr(bits, (int64_t)blockIdx.z * ws_stride);
+  sums = shift_ptr(sums, (int64_t)blockIdx.z * ws_stride);
   const int lane = threadIdx.x & 31;
   const int64_t warp = first_chunk + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -476,7 +497,52 @@ struct FeIsoWs {
 
 struct FeWsAll {
   FeIsoWs iso[TKMC_MAX_ISO];
+  // A batch of blocks of one shape (blockIdx.z = block): their workspaces
+  // `stride` bytes apart, and per block its volume, mask (entries may be
+  // null) and geometry {x0, y0, z0, dx, dy, dz}.  stride = 0 and null
+  // tables for one volume.
+  int64_t stride;
+  const float* const* vols;
+  const int32_t* const* masks;
+  const float* geoms;
 };
+
+// Workspace views of isovalue q for this CTA's block of a batch.
+__device__ __forceinline__ FeIsoWs iso_ws(const FeWsAll& ws, int q) {
+  FeIsoWs w = ws.iso[q];
+  if (ws.stride) {
+    const int64_t off = (int64_t)blockIdx.z * ws.stride;
+    w.bits = shift_ptr(w.bits, off);
+    w.sums = shift_ptr(w.sums, off);
+    w.cnt = shift_ptr(w.cnt, off);
+    w.wact = shift_ptr(w.wact, off);
+    w.tot = shift_ptr(w.tot, off);
+    w.rowoff = shift_ptr(w.rowoff, off);
+    w.work = shift_ptr(w.work, off);
+    w.ufirst = shift_ptr(w.ufirst, off);
+    w.ucnt = shift_ptr(w.ucnt, off);
+    w.wcnt = shift_ptr(w.wcnt, off);
+    w.units = shift_ptr(w.units, off);
+    w.flags = shift_ptr(w.flags, off);
+    w.super = shift_ptr(w.super, off);
+    w.agg = shift_ptr(w.agg, off);
+    w.incl = shift_ptr(w.incl, off);
+    w.info = shift_ptr(w.info, off);
+  }
+  return w;
+}
+
+// This CTA's block's mask, volume and geometry (the launch's own for one
+// volume).
+__device__ __forceinline__ const int32_t* block_mask(const FeWsAll& ws, const int32_t* mask) {
+  return ws.vols ? (ws.masks ? ws.masks[blockIdx.z] : nullptr) : mask;
+}
+__device__ __forceinline__ const float* block_vol(const FeWsAll& ws, const float* v) {
+  return ws.vols ? ws.vols[blockIdx.z] : v;
+}
+__device__ __forceinline__ const float* block_geom(const FeWsAll& ws, const float* g) {
+  return ws.geoms ? ws.geoms + 6 * (int64_t)blockIdx.z : g;
+}
 
 // Bits of four node rows around one word: a = (j,k), b = (j+1,k),
 // c = (j,k+1), d = (j+1,k+1), each with the next word's bit 0 available
@@ -730,7 +796,8 @@ __global__ void __launch_bounds__(kThreads, 3)
 k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nwords) {
   extern __shared__ uint32_t k2_smem[];
   __shared__ int s_ntri[256];
-  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
+  const int32_t* __restrict__ mask_b = block_mask(ws, mask);
   const int tid = threadIdx.x;
   const int TR = d.TR, W = d.W;
   const int64_t stage = k2_stage_words(TR, W);
@@ -756,9 +823,9 @@ k_fe_count(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask, int64_t nword
   cp_async_wait_all();
   __syncthreads();
   if ((L & 31) == 0)
-    count_rows<true>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
+    count_rows<true>(d, Wk, mask_b, s_ntri, sAr, sCr, R0, a_first, c_first);
   else
-    count_rows<false>(d, Wk, mask, s_ntri, sAr, sCr, R0, a_first, c_first);
+    count_rows<false>(d, Wk, mask_b, s_ntri, sAr, sCr, R0, a_first, c_first);
 }
 
 // Position of the k-th (0-based) set bit of m; k < popc(m).
@@ -960,7 +1027,8 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   __shared__ unsigned s_nu[kThreads];
   __shared__ uint32_t s_act[kThreads];
   __shared__ long long s_red[5][kThreads / 32];
-  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
+  const int32_t* __restrict__ mask_b = block_mask(ws, mask);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256
 #pragma unroll
@@ -998,7 +1066,7 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
         const int wb = nth_set_bit(ocand, (int)(e - opre));
         w = 32 * g + wb;
         const RowQuad oq = row_quad(d, rbase + own);
-        c = count_word(load_word_quad(Wk.bits, oq, w, W), oq, w, Li, d, mask, s_ntri);
+        c = count_word(load_word_quad(Wk.bits, oq, w, W), oq, w, Li, d, mask_b, s_ntri);
       }
       if (c != 0u) {
         const int rl = warp * 32 + own;
@@ -1058,7 +1126,7 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, int64_t unit_cap, int rows_only) {
   __shared__ long long s_w[5][kThreads / 32];
   __shared__ long long s_pre[5], s_all[5];
   __shared__ long long s_run[kThreads / 32][32][4];
-  const FeIsoWs& Wk = ws.iso[blockIdx.y];
+  const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t tile = blockIdx.x;
   const int64_t rbase = tile * kThreads + warp * 32;  // the warp's first row
@@ -1215,7 +1283,7 @@ k_fe_scan_rows(FeDims d, FeWsAll ws, int64_t wait_ns, int64_t skip_tile) {
   __shared__ long long s_prefix[4];
   __shared__ int64_t s_tile;
   __shared__ unsigned s_wbase[kThreads / 32];
-  const FeIsoWs& W = ws.iso[blockIdx.y];
+  const FeIsoWs W = iso_ws(ws, blockIdx.y);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (tid == 0) s_tile = (int64_t)atomicAdd((unsigned long long*)(W.info + 9), 1ull);
   __syncthreads();
@@ -1407,7 +1475,11 @@ k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint32_t s_rec[kThreads / 32][32 * kRec];
   __shared__ long long s_tri[kThreads / 32][32];  // running triangle offset per row segment
   const int isoi = blockIdx.y;
-  const FeIsoWs& W = ws.iso[isoi];
+  const FeIsoWs W = iso_ws(ws, isoi);
+  const float* __restrict__ vol = block_vol(ws, A.v);
+  const int32_t* __restrict__ msk = block_mask(ws, A.mask);
+  const float* gm = block_geom(ws, A.geom);
+  const int bq = (int)blockIdx.z * (int)gridDim.y + isoi;  // bases of this block and isovalue
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_tris[tid];
   __syncthreads();
@@ -1422,13 +1494,13 @@ k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const float iso = A.iso.v[isoi];
-  const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
-  const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idB[3] = {base_id(A, isoi, 0), base_id(A, isoi, 1), base_id(A, isoi, 2)};
-  const long long shiftX = base_out(A, isoi, 0) - idB[0];
-  const long long shiftY = base_out(A, isoi, 1) - idB[1];
-  const long long shiftZ = base_out(A, isoi, 2) - idB[2];
-  const long long outT = base_tri(A, isoi);
+  const float x0 = gm[0], y0 = gm[1], z0 = gm[2];
+  const float hx = gm[3], hy = gm[4], hz = gm[5];
+  const long long idB[3] = {base_id(A, bq, 0), base_id(A, bq, 1), base_id(A, bq, 2)};
+  const long long shiftX = base_out(A, bq, 0) - idB[0];
+  const long long shiftY = base_out(A, bq, 1) - idB[1];
+  const long long shiftZ = base_out(A, bq, 2) - idB[2];
+  const long long outT = base_tri(A, bq);
 
   for (int64_t grp = gw; grp * G < n_active; grp += nw) {
     // ---------------- phase 1: lane = (row segment, word) ----------------
@@ -1544,7 +1616,7 @@ k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
           const int64_t n = 32 * (int64_t)(w0 + (u & (S - 1))) + bit;
           const int64_t node = ((int64_t)uk * d.M + uj) * L + n;
           const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
-          const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
+          const float s0 = __ldg(vol + node), s1 = __ldg(vol + node + step);
           const long long shift = type == 0 ? shiftX : (type == 1 ? shiftY : shiftZ);
           const long long row = rec_i64(R, kRecOff + 2 * type) +
                                 __popc(mm & ((1u << bit) - 1u)) + shift;
@@ -1587,9 +1659,9 @@ k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
                                    R[kRecBits + 6], R[kRecBits + 7]);
           pkc = s_case[cs];
           nt = (unsigned)(pkc >> 60);
-          if (nt && A.mask) {
+          if (nt && msk) {
             const int64_t cell = ((int64_t)R[kRecK] * d.ny + R[kRecJ]) * d.nx + n;
-            if (__ldg(A.mask + cell) != 0) nt = 0;
+            if (__ldg(msk + cell) != 0) nt = 0;
           }
         }
         // Exclusive scan of nt within each run of lanes of one row.
@@ -1730,7 +1802,11 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
   EmitSmem& S = *reinterpret_cast<EmitSmem*>(k3_smem);
   const int isoi = blockIdx.y;
-  const FeIsoWs& W = ws.iso[isoi];
+  const FeIsoWs W = iso_ws(ws, isoi);
+  const float* __restrict__ vol = block_vol(ws, A.v);
+  const int32_t* __restrict__ msk = block_mask(ws, A.mask);
+  const float* gm = block_geom(ws, A.geom);
+  const int bq = (int)blockIdx.z * (int)gridDim.y + isoi;  // bases of this block and isovalue
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_tris[tid];
   __syncthreads();
@@ -1744,14 +1820,14 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5;
   const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
   const float iso = A.iso.v[isoi];
-  const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
-  const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idX = base_id(A, isoi, 0), idY = base_id(A, isoi, 1),
-                  idZ = base_id(A, isoi, 2);
-  const long long shiftX = base_out(A, isoi, 0) - idX;
-  const long long shiftY = base_out(A, isoi, 1) - idY;
-  const long long shiftZ = base_out(A, isoi, 2) - idZ;
-  const long long outT = base_tri(A, isoi);
+  const float x0 = gm[0], y0 = gm[1], z0 = gm[2];
+  const float hx = gm[3], hy = gm[4], hz = gm[5];
+  const long long idX = base_id(A, bq, 0), idY = base_id(A, bq, 1),
+                  idZ = base_id(A, bq, 2);
+  const long long shiftX = base_out(A, bq, 0) - idX;
+  const long long shiftY = base_out(A, bq, 1) - idY;
+  const long long shiftZ = base_out(A, bq, 2) - idZ;
+  const long long outT = base_tri(A, bq);
 
   for (int64_t grp = gw; grp * 32 < n_active; grp += nw) {
     // ---- rows: lane = one active row ----
@@ -1849,13 +1925,13 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
           const uint32_t un = (an ^ bn) | (an ^ cn) | (an ^ dn);
           act = (u | (u >> 1) | (un << 31) | (qa ^ qa1)) & xm;
           ntu = tri_count_word(qa, qa1, qb, qb1, qc, qc1, qd, qd1, xm);
-          if (A.mask && act) {
+          if (msk && act) {
             const int64_t cell0 = ((int64_t)sk * d.ny + sj) * d.nx + 32 * (int64_t)w;
             uint32_t t = act;
             while (t) {
               const int bit = __ffs(t) - 1;
               t &= t - 1;
-              if (__ldg(A.mask + cell0 + bit) != 0) {
+              if (__ldg(msk + cell0 + bit) != 0) {
                 ntu -= (unsigned)(s_case[cell_case(bit, qa, qa1, qb, qb1, qc, qc1, qd, qd1)] >> 60);
                 act &= ~(1u << bit);
               }
@@ -1939,7 +2015,7 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
           const int64_t n = 32 * (int64_t)R[kURW] + bit;
           const int64_t node = ((int64_t)uk * d.M + uj) * L + n;
           const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
-          const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
+          const float s0 = __ldg(vol + node), s1 = __ldg(vol + node + step);
           const long long shift = type == 0 ? shiftX : (type == 1 ? shiftY : shiftZ);
           const long long row = ld_i64(R + kUROff + 2 * type) + __popc(mm & ((1u << bit) - 1u)) +
                                 shift;
@@ -2060,7 +2136,11 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
   __shared__ long long s_tri[kThreads / 32][32];
   const int isoi = blockIdx.y;
-  const FeIsoWs& W = ws.iso[isoi];
+  const FeIsoWs W = iso_ws(ws, isoi);
+  const float* __restrict__ vol = block_vol(ws, A.v);
+  const int32_t* __restrict__ msk = block_mask(ws, A.mask);
+  const float* gm = block_geom(ws, A.geom);
+  const int bq = (int)blockIdx.z * (int)gridDim.y + isoi;  // bases of this block and isovalue
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   s_case[tid] = c_case_groups[tid];  // kThreads == 256
   __syncthreads();
@@ -2071,13 +2151,13 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const int64_t L = d.L, plane = d.L * d.M;
   const uint32_t M32 = (uint32_t)d.M;
   const float iso = A.iso.v[isoi];
-  const float x0 = A.geom[0], y0 = A.geom[1], z0 = A.geom[2];
-  const float hx = A.geom[3], hy = A.geom[4], hz = A.geom[5];
-  const long long idX = base_id(A, isoi, 0), idY = base_id(A, isoi, 1),
-                  idZ = base_id(A, isoi, 2);
-  const long long shX = base_out(A, isoi, 0) - idX, shY = base_out(A, isoi, 1) - idY,
-                  shZ = base_out(A, isoi, 2) - idZ;
-  const long long outT = base_tri(A, isoi);
+  const float x0 = gm[0], y0 = gm[1], z0 = gm[2];
+  const float hx = gm[3], hy = gm[4], hz = gm[5];
+  const long long idX = base_id(A, bq, 0), idY = base_id(A, bq, 1),
+                  idZ = base_id(A, bq, 2);
+  const long long shX = base_out(A, bq, 0) - idX, shY = base_out(A, bq, 1) - idY,
+                  shZ = base_out(A, bq, 2) - idZ;
+  const long long outT = base_tri(A, bq);
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t grp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5; grp * 32 < n_own;
        grp += nwarps) {
@@ -2181,7 +2261,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
         const int64_t n = 32 * (int64_t)R[kUW] + bit;
         const int64_t node = (int64_t)R[kURow] * L + n;
         const int64_t step = type == 0 ? 1 : (type == 1 ? L : plane);
-        const float s0 = __ldg(A.v + node), s1 = __ldg(A.v + node + step);
+        const float s0 = __ldg(vol + node), s1 = __ldg(vol + node + step);
         const long long row = (long long)R[kUB + type] + kk +
                               (type == 0 ? shX : (type == 1 ? shY : shZ));
         if (row < 0 || row >= A.points_cap) {
@@ -2214,10 +2294,10 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
         const uint32_t* R = U + ui * kUS;
         cb = nth_set_bit(R[kUAct], (int)(ce - R[kUPC]));
         bool masked = false;
-        if (A.mask) {
+        if (msk) {
           const int64_t r = R[kURow];
           const uint32_t j = (uint32_t)r % M32, k = (uint32_t)r / M32;
-          masked = __ldg(A.mask + ((int64_t)k * d.ny + j) * d.nx + 32 * (int64_t)R[kUW] + cb) != 0;
+          masked = __ldg(msk + ((int64_t)k * d.ny + j) * d.nx + 32 * (int64_t)R[kUW] + cb) != 0;
         }
         if (!masked) {
           pkc = s_case[cell_case(cb, R[kUQ + 0], R[kUQ + 1], R[kUQ + 2], R[kUQ + 3], R[kUQ + 4],
@@ -3118,11 +3198,11 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
     if (niso == 1)
       k_fe_threshold_v4<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
                                                            f.bits_stride, f.nwords, sums0,
-                                                           f.sums_stride, nchunks);
+                                                           f.sums_stride, nchunks, 0, nullptr);
     else
       k_fe_threshold_multi<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
                                                               f.bits_stride, f.nwords, sums0,
-                                                              f.sums_stride, nchunks);
+                                                              f.sums_stride, nchunks, 0, nullptr);
     TK_LAUNCHED();
   }
   if (nfull < nchunks) {  // unaligned volume, or the ragged last chunk
@@ -3131,7 +3211,7 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
     if (gb > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
     k_fe_threshold_scalar<<<(unsigned)gb, kThreads, 0, st>>>(scalar, f.V, iso, niso, bits0,
                                                              f.bits_stride, f.nwords, sums0,
-                                                             f.sums_stride, nfull);
+                                                             f.sums_stride, nfull, 0, nullptr);
     TK_LAUNCHED();
   }
   return TKMC_OK;
@@ -3361,6 +3441,130 @@ int tkmc_fe_emit_soup(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
                      st>>>(f.d, v, A, out_x, out_y, out_z);
     TK_LAUNCHED();
   }
+  return TKMC_OK;
+}
+
+// ---- batches of same-shape blocks ----------------------------------------
+
+size_t tkmc_fe_batch_stride(int64_t nx, int64_t ny, int64_t nz, int niso) {
+  return align_up(tkmc_fe_workspace_bytes(nx, ny, nz, niso), 256);
+}
+
+static int batch_views(int64_t nx, int64_t ny, int64_t nz, int niso, int64_t nblocks,
+                       const float* const* vols, const int32_t* const* masks, void* ws,
+                       size_t ws_bytes, FeLayout* f, FeWsAll* v) {
+  if (nblocks < 1 || nblocks > 65535)
+    return set_err(TKMC_ERR_INVALID_ARG, "nblocks must be in [1, 65535], got %lld",
+                   (long long)nblocks);
+  if (!fe_layout(nx, ny, nz, 0, niso, f)) return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  if (!vols) return set_err(TKMC_ERR_INVALID_ARG, "vols is NULL");
+  const size_t stride = align_up(f->total, 256);
+  int rc = check_ws(ws, ws_bytes, stride * (size_t)nblocks);
+  if (rc) return rc;
+  *v = fe_views(*f, ws, niso);
+  v->stride = (int64_t)stride;
+  v->vols = vols;
+  v->masks = masks;
+  return TKMC_OK;
+}
+
+int tkmc_fe_count_batch(const float* const* vols, int64_t nblocks, int64_t nx, int64_t ny,
+                        int64_t nz, const float* isovalues, int niso, const int32_t* const* masks,
+                        void* ws, size_t ws_bytes, int64_t* counts, int64_t* status,
+                        void* stream) {
+  int rc = check_iso(isovalues, niso);
+  if (rc) return rc;
+  FeLayout f;
+  FeWsAll v;
+  if ((rc = batch_views(nx, ny, nz, niso, nblocks, vols, masks, ws, ws_bytes, &f, &v))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  IsoParams iso{};
+  for (int t = 0; t < niso; ++t) iso.v[t] = isovalues[t];
+  const int64_t nchunks = (f.V + 1023) / 1024, nfull = f.V / 1024;
+  constexpr int kWarps = kThreads / 32;
+  const unsigned nb = (unsigned)nblocks;
+  // Device pointers of unknown alignment: the scalar-load layout for full
+  // chunks, the scalar kernel for a ragged last chunk.
+  if (nfull > 0) {
+    k_fe_threshold_multi<<<dim3((unsigned)((nfull + kWarps - 1) / kWarps), 1, nb), kThreads, 0, st>>>(
+        nullptr, nfull, iso, niso, v.iso[0].bits, f.bits_stride, f.nwords, v.iso[0].sums,
+        f.sums_stride, nchunks, v.stride, vols);
+    TK_LAUNCHED();
+  }
+  if (nfull < nchunks) {
+    k_fe_threshold_scalar<<<dim3(1, 1, nb), kThreads, 0, st>>>(
+        nullptr, f.V, iso, niso, v.iso[0].bits, f.bits_stride, f.nwords, v.iso[0].sums,
+        f.sums_stride, nfull, v.stride, vols);
+    TK_LAUNCHED();
+  }
+  TK_CUDA(cudaMemset2DAsync(static_cast<char*>(ws) + f.off_info, (size_t)v.stride, 0,
+                            f.reset_bytes - f.off_info, (size_t)nblocks, st));
+  if ((f.d.L & 31) == 0) {
+    const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso, nb);
+    k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, nullptr);
+    TK_LAUNCHED();
+    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, f.unit_cap, 0);
+    TK_LAUNCHED();
+  } else {
+    if (f.k2_smem > 48 * 1024)
+      if ((rc = ensure_smem(k_fe_count, f.k2_smem, g_smem_count))) return rc;
+    k_fe_count<<<dim3((unsigned)f.d.ctiles, (unsigned)niso, nb), kThreads, f.k2_smem, st>>>(
+        f.d, v, nullptr, f.nwords);
+    TK_LAUNCHED();
+    k_fe_scan_rows<<<dim3((unsigned)f.d.ntiles, (unsigned)niso, nb), kThreads, 0, st>>>(
+        f.d, v, g_wait_ns.load(), -1);
+    TK_LAUNCHED();
+  }
+  for (int q = 0; q < niso; ++q) {
+    const char* info = static_cast<const char*>(ws) + f.off_info + (size_t)q * 16 * 8;
+    if (counts)
+      TK_CUDA(cudaMemcpy2DAsync(counts + 4 * q, (size_t)niso * 4 * 8, info, (size_t)v.stride, 4 * 8,
+                                (size_t)nblocks, cudaMemcpyDefault, st));
+    if (status)
+      TK_CUDA(cudaMemcpy2DAsync(status + q, (size_t)niso * 8, info + 10 * 8, (size_t)v.stride, 8,
+                                (size_t)nblocks, cudaMemcpyDefault, st));
+  }
+  return TKMC_OK;
+}
+
+int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx, int64_t ny,
+                       int64_t nz, const float* geoms, const float* isovalues, int niso,
+                       const int32_t* const* masks, void* ws, size_t ws_bytes,
+                       const int64_t* bases, float* points, int64_t points_capacity,
+                       int32_t* conn, int64_t conn_capacity, int64_t* status, void* stream) {
+  int rc = check_iso(isovalues, niso);
+  if (rc) return rc;
+  FeLayout f;
+  FeWsAll v;
+  if ((rc = batch_views(nx, ny, nz, niso, nblocks, vols, masks, ws, ws_bytes, &f, &v))) return rc;
+  if (!geoms || !bases) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_emit_batch: NULL argument");
+  v.geoms = geoms;
+  FeEmitArgs A{};
+  A.points = points;
+  A.conn = conn;
+  A.points_cap = points ? points_capacity : 0;
+  A.conn_cap = conn ? conn_capacity : 0;
+  A.dev_bases = reinterpret_cast<const long long*>(bases);
+  for (int q = 0; q < niso; ++q) A.iso.v[q] = isovalues[q];
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned nb = (unsigned)nblocks;
+  const int per_block =
+      (int)std::max<int64_t>(1, std::min<int64_t>(64, (int64_t)sm_count() * 8 / nblocks));
+  if (f.unit_cap > 0) {
+    k_fe_emit_units<<<dim3((unsigned)per_block, (unsigned)niso, nb), kThreads, 0, st>>>(f.d, v, A);
+  } else if (f.d.AW <= kMaxAW) {
+    const size_t smem = sizeof(EmitSmem);
+    if ((rc = ensure_smem(k_fe_emit_words, smem, g_smem_emit_words))) return rc;
+    k_fe_emit_words<<<dim3((unsigned)per_block, (unsigned)niso, nb), kThreads, smem, st>>>(f.d, v, A);
+  } else {
+    k_fe_emit_rows<<<dim3((unsigned)per_block, (unsigned)niso, nb), kThreads, 0, st>>>(f.d, v, A);
+  }
+  TK_LAUNCHED();
+  if (status)
+    for (int q = 0; q < niso; ++q)
+      TK_CUDA(cudaMemcpy2DAsync(status + q, (size_t)niso * 8,
+                                static_cast<const char*>(ws) + f.off_info + (size_t)q * 16 * 8 + 10 * 8,
+                                (size_t)v.stride, 8, (size_t)nblocks, cudaMemcpyDefault, st));
   return TKMC_OK;
 }
 

@@ -302,3 +302,38 @@ def test_many_blocks_match_oracle(tack, oracle):
     assert_points_identical(r["points"], ref["points"])
     assert r["block_point_counts"] == list(ref["block_point_counts"])
     assert r["block_tri_counts"] == list(ref["block_tri_counts"])
+
+
+@pytest.mark.parametrize("cells,nblocks", [((31, 31, 31), 27), ((32, 32, 32), 27), ((7, 5, 3), 200)])
+def test_block_batches_match_oracle(tack, oracle, cells, nblocks):
+    """Blocks of one shape go through the batched count and emit (rows of a
+    multiple of 32 nodes and not, tiny blocks of one partial chunk), with
+    masks on some blocks and several isovalues; equal to the oracle's
+    flying_edges_multiblock per isovalue, concatenated."""
+    nx, ny, nz = cells
+    rng = np.random.default_rng(nx * 7 + nblocks)
+    n = (nx + 1) * (ny + 1) * (nz + 1)
+    blocks_gpu, blocks_ref = [], []
+    for b in range(nblocks):
+        i = np.arange(n)
+        v = (np.sin(i * 0.013 + b) + 0.4 * rng.standard_normal(n)).astype(np.float32)
+        g = (nx, ny, nz, float(b % 3) * nx, float(b // 3 % 3) * ny, float(b // 9) * nz,
+             0.5, 0.75, 1.0)
+        blk = {"scalar": _upload(tack, v, tack.f32), "grid": tack.UniformGrid(*g)}
+        ref = {"values": v, "grid": oracle.Grid(*g)}
+        if b % 5 == 2:
+            m = (rng.random(nx * ny * nz) < 0.4).astype(np.int32)
+            blk["mask"] = _upload(tack, m, tack.i32)
+            ref["mask"] = m
+        blocks_gpu.append(blk)
+        blocks_ref.append(ref)
+    isos = [0.1, -0.5]
+    r = tack.flying_edges_multiblock(blocks_gpu, isos)
+    pts, conns, p0 = [], [], 0
+    for iso in isos:
+        ref = oracle.flying_edges_multiblock(blocks_ref, iso)
+        pts.append(ref["points"])
+        conns.append(ref["conn"] + p0)
+        p0 += ref["points"].shape[0]
+    np.testing.assert_array_equal(r["conn"], np.concatenate(conns))
+    assert_points_identical(r["points"], np.concatenate(pts))
