@@ -60,6 +60,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="totals exchange between ranks (N>1): NVLink peer stores or NCCL")
     return ap.parse_args()
 
 
@@ -258,7 +260,7 @@ def main():
     grid = tack.UniformGrid(nxn - 1, nyn - 1, nzn - 1, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
     vol = workloads.generate(args.config, shape, plan.k0, plan.k1, device=dev)
     torch.cuda.synchronize()
-    eng = SlabEngine(grid, plan, isos)
+    eng = SlabEngine(grid, plan, isos, exchange=args.exchange)
     lib = _lib.load()
     stream = torch.cuda.current_stream(dev)
     niso = len(isos)
@@ -386,7 +388,8 @@ def main():
             "config": {
                 "workload": workload_name(args.config, shape, isos),
                 "volume_nodes": list(shape), "cells": cells, "isovalues": isos,
-                "parallelism": (f"z-slab x{world} (ghost plane, one NCCL all-gather of totals)"
+                "parallelism": (f"z-slab x{world} (ghost plane; totals exchanged by "
+                                f"{'NVLink peer stores' if args.exchange == 'p2p' else 'NCCL all-gather'})"
                                 if world > 1 else "single GPU"),
                 "l2": (f"inputs larger than L2 (f32 slab {4.0 * local_nodes / 2**30:.2f} GiB per "
                        f"GPU vs 126 MB L2), no flush" if 4.0 * local_nodes > 126e6 * 2 else
@@ -417,6 +420,7 @@ def main():
             "cpu_baseline": cpu,
         }
         print(json.dumps(out), flush=True)
+    eng.close()
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -259,6 +259,30 @@ int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx,
                        float* points, int64_t points_capacity, int32_t* conn,
                        int64_t conn_capacity, int64_t* status, void* stream);
 
+/* ---- totals exchange over NVLink peer memory ----------------------------- */
+/*
+ * For z-slab ranks, one GPU and one process each: instead of an NCCL
+ * all-gather of the totals followed by tkmc_fe_plan, one kernel stores this
+ * rank's totals straight into every rank's memory (CUDA IPC mappings over
+ * NVLink), raises a per-call epoch flag in each, waits (bounded; a wait that
+ * runs out records TKMC_ERR_DEVICE_TIMEOUT, read by tkmc_fe_check) for every
+ * rank's flag, and plans.  Every rank must make the same calls in the same
+ * order, on its own GPU.  No counterpart in the reference (it has no
+ * multi-GPU path).
+ *   create: allocate this rank's exchange buffer; writes its IPC handle
+ *           (tkmc_exchange_handle_bytes bytes) for the other ranks.
+ *   connect: open every rank's handle (handles in rank order).
+ *   plan: after tkmc_fe_scan on this rank's slab; bases_dev as tkmc_fe_plan.
+ *   destroy: after every rank has finished its last plan (a barrier).
+ */
+size_t tkmc_exchange_handle_bytes(void);
+int tkmc_exchange_create(int world, int rank, int niso, void** exchange, void* handle);
+int tkmc_exchange_connect(void* exchange, const void* handles);
+int tkmc_exchange_plan(void* exchange, int64_t nx, int64_t ny, int64_t nz,
+                       int ghost_plane, const void* workspace, size_t workspace_bytes,
+                       int shared_output, int64_t* bases_dev, void* stream);
+int tkmc_exchange_destroy(void* exchange);
+
 /* Copy the device status word of each isovalue (niso int64: 0, or the
  * TKMC_ERR_* code the last count/emit recorded -- TKMC_ERR_DEVICE_TIMEOUT,
  * TKMC_ERR_CAPACITY) to dst (device or page-locked host memory), so that

@@ -48,6 +48,11 @@ SIGNATURES = {
     "tkmc_fe_count_batch": (_I, [_P, _I64, _I64, _I64, _I64, _P, _I, _P, _P, _SZ, _P, _P, _P]),
     "tkmc_fe_emit_batch": (_I, [_P, _I64, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P,
                                 _I64, _P, _I64, _P, _P]),
+    "tkmc_exchange_handle_bytes": (_SZ, []),
+    "tkmc_exchange_create": (_I, [_I, _I, _I, _P, _P]),
+    "tkmc_exchange_connect": (_I, [_P, _P]),
+    "tkmc_exchange_plan": (_I, [_P, _I64, _I64, _I64, _I, _P, _SZ, _I, _P, _P]),
+    "tkmc_exchange_destroy": (_I, [_P]),
     "tkmc_fe_emit_soup": (_I, [_P, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P,
                                _I64, _P]),
     "tkmc_fe_plan": (_I, [_P, _I, _I, _I, _I, _P, _P]),

@@ -2459,9 +2459,8 @@ k_fe_emit_soup(FeDims d, FeWsAll ws, FeEmitArgs A, float* __restrict__ ox,
 // ranks' x points, then all y, then all z), and rows in the rank-local
 // output (isovalue-major; x, y, z sections of this rank).  The same sums as
 // the host's slab_bases.
-__global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, int niso,
-                          int shared_output, long long* __restrict__ bases) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+__device__ void k_fe_plan_body(const long long* c, int world, int rank, int niso,
+                               int shared_output, long long* bases) {
   long long Pq = 0, Tq = 0, lp = 0, lt = 0;
   for (int q = 0; q < niso; ++q) {
     long long tot[4] = {0, 0, 0, 0}, before[4] = {0, 0, 0, 0}, own[4];
@@ -2493,6 +2492,80 @@ __global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, 
     lt += own[3];
   }
 }
+
+__global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, int niso,
+                          int shared_output, long long* __restrict__ bases) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) k_fe_plan_body(c, world, rank, niso, shared_output, bases);
+}
+
+// ------------------------------------------------------------------------
+// totals exchange over NVLink peer memory (z-slab ranks, one GPU each)
+// ------------------------------------------------------------------------
+//
+// Every rank keeps a `gathered` array [world][niso][4] and a flag per peer in
+// its own memory, mapped into every other rank (CUDA IPC).  One warp per
+// rank: bump the local epoch, store this rank's totals into slot `rank` of
+// every rank's gathered array (stores over NVLink), fence, then release
+// flags[rank] = epoch into every rank; wait (bounded by %globaltimer) until
+// all flags of the local array reach the epoch, then plan from the local
+// gathered array exactly as k_fe_plan does.  A wait that runs out records
+// TKMC_ERR_DEVICE_TIMEOUT in the workspace and plans from what is there.
+constexpr int kMaxRanks = 32;
+
+struct ExchangePeers {
+  long long* gathered[kMaxRanks];            // each rank's gathered array (peer pointers)
+  unsigned long long* flags[kMaxRanks];      // each rank's flags (peer pointers)
+};
+
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoch, int world,
+                                   int rank, int niso, const long long* __restrict__ own_info,
+                                   int shared_output, long long* __restrict__ bases,
+                                   long long* err, int64_t wait_ns) {
+  const int lane = threadIdx.x;  // one warp
+  __shared__ unsigned long long s_epoch;
+  if (lane == 0) s_epoch = ++(*epoch);
+  __syncwarp();
+  const unsigned long long ep = s_epoch;
+  // This rank's totals {X, Y, Z, T} per isovalue (info[16 q + 0..3]) into
+  // slot `rank` of every rank's gathered array.
+  for (int r = lane; r < world; r += 32) {
+    long long* dst = peers.gathered[r] + (int64_t)rank * niso * 4;
+    for (int q = 0; q < niso; ++q)
+      for (int t = 0; t < 4; ++t) dst[4 * q + t] = own_info[16 * q + t];
+  }
+  __threadfence_system();
+  __syncwarp();
+  for (int r = lane; r < world; r += 32) st_release_sys_u64(peers.flags[r] + rank, ep);
+  // Wait for every rank's totals in the local array.
+  const unsigned long long* mine = peers.flags[rank];
+  bool ok = true;
+  for (int r = lane; r < world; r += 32) {
+    if (ld_acquire_sys_u64(mine + r) >= ep) continue;
+    const uint64_t t0 = global_ns();
+    while (ld_acquire_sys_u64(mine + r) < ep) {
+      if ((int64_t)(global_ns() - t0) > wait_ns) {
+        ok = false;
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  if (!__all_sync(0xffffffffu, ok) && lane == 0)
+    atomicExch((unsigned long long*)err, (unsigned long long)TKMC_ERR_DEVICE_TIMEOUT);
+  __syncwarp();
+  if (lane == 0)
+    k_fe_plan_body(peers.gathered[rank], world, rank, niso, shared_output, bases);
+}
+
 
 // Forget capacity errors recorded by an emit (device timeouts stay).
 __global__ void k_fe_clear_capacity_error(FeWsAll ws, int niso) {
@@ -3565,6 +3638,92 @@ int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx, in
       TK_CUDA(cudaMemcpy2DAsync(status + q, (size_t)niso * 8,
                                 static_cast<const char*>(ws) + f.off_info + (size_t)q * 16 * 8 + 10 * 8,
                                 (size_t)v.stride, 8, (size_t)nblocks, cudaMemcpyDefault, st));
+  return TKMC_OK;
+}
+
+// ---- totals exchange over NVLink peer memory ------------------------------
+
+struct tkmc_exchange_impl {
+  int world, rank, niso, device;
+  char* base;  // one allocation: flags [world] u64 | gathered [world][niso][4] i64 | epoch u64
+  size_t off_gathered, off_epoch, bytes;
+  ExchangePeers peers;
+  void* opened[kMaxRanks];
+};
+
+size_t tkmc_exchange_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int tkmc_exchange_create(int world, int rank, int niso, void** out, void* handle) {
+  if (!out || !handle) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_create: NULL argument");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || niso < 1 ||
+      niso > TKMC_MAX_ISO)
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_create: bad world/rank/niso");
+  tkmc_exchange_impl* x = new tkmc_exchange_impl();
+  x->world = world;
+  x->rank = rank;
+  x->niso = niso;
+  cudaError_t e = cudaGetDevice(&x->device);
+  x->off_gathered = align_up((size_t)world * 8, 256);
+  x->off_epoch = x->off_gathered + align_up((size_t)world * niso * 4 * 8, 256);
+  x->bytes = x->off_epoch + 256;
+  if (e == cudaSuccess) e = cudaMalloc(&x->base, x->bytes);
+  if (e == cudaSuccess) e = cudaMemset(x->base, 0, x->bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), x->base);
+  if (e != cudaSuccess) {
+    if (x->base) cudaFree(x->base);
+    delete x;
+    return set_err(TKMC_ERR_CUDA, "tkmc_exchange_create: %s", cudaGetErrorString(e));
+  }
+  *out = x;
+  return TKMC_OK;
+}
+
+int tkmc_exchange_connect(void* xp, const void* handles) {
+  tkmc_exchange_impl* x = static_cast<tkmc_exchange_impl*>(xp);
+  if (!x || !handles) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_connect: NULL argument");
+  const cudaIpcMemHandle_t* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < x->world; ++r) {
+    char* b = x->base;
+    if (r != x->rank) {
+      void* p = nullptr;
+      const cudaError_t e = cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess)
+        return set_err(TKMC_ERR_CUDA, "tkmc_exchange_connect: rank %d: %s", r, cudaGetErrorString(e));
+      x->opened[r] = p;
+      b = static_cast<char*>(p);
+    }
+    x->peers.flags[r] = reinterpret_cast<unsigned long long*>(b);
+    x->peers.gathered[r] = reinterpret_cast<long long*>(b + x->off_gathered);
+  }
+  return TKMC_OK;
+}
+
+int tkmc_exchange_plan(void* xp, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                       const void* ws, size_t ws_bytes, int shared_output, int64_t* bases_dev,
+                       void* stream) {
+  tkmc_exchange_impl* x = static_cast<tkmc_exchange_impl*>(xp);
+  if (!x || !bases_dev) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_plan: NULL argument");
+  FeLayout f;
+  if (!fe_layout(nx, ny, nz, ghost_plane, x->niso, &f))
+    return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
+  int rc = check_ws(const_cast<void*>(ws), ws_bytes, f.total);
+  if (rc) return rc;
+  const long long* info = reinterpret_cast<const long long*>(static_cast<const char*>(ws) + f.off_info);
+  k_fe_exchange_plan<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      x->peers, reinterpret_cast<unsigned long long*>(x->base + x->off_epoch), x->world, x->rank,
+      x->niso, info, shared_output, reinterpret_cast<long long*>(bases_dev),
+      const_cast<long long*>(info) + 10, g_wait_ns.load());
+  TK_LAUNCHED();
+  return TKMC_OK;
+}
+
+int tkmc_exchange_destroy(void* xp) {
+  tkmc_exchange_impl* x = static_cast<tkmc_exchange_impl*>(xp);
+  if (!x) return TKMC_OK;
+  for (int r = 0; r < x->world; ++r)
+    if (x->opened[r]) cudaIpcCloseMemHandle(x->opened[r]);
+  cudaFree(x->base);
+  delete x;
   return TKMC_OK;
 }
 

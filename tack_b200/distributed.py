@@ -117,11 +117,19 @@ def _f32(vals):
 class SlabEngine:
     """Per-rank state: plan, workspace and the collective used for totals."""
 
-    def __init__(self, grid, plan, isovalues, group=None):
+    def __init__(self, grid, plan, isovalues, group=None, exchange="nccl"):
+        """exchange: how run_device shares the totals between ranks --
+        "nccl" (an all-gather into device buffers) or "p2p" (one kernel
+        storing into every rank's memory over NVLink; needs one GPU per rank
+        and CUDA IPC between the processes)."""
         if len(isovalues) > _lib.MAX_ISO:
             raise ValueError(f"at most {_lib.MAX_ISO} isovalues per slab call")
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"unknown exchange {exchange!r}")
         self.grid, self.plan, self.isos = grid, plan, list(isovalues)
         self.group = group
+        self.exchange_kind = exchange
+        self._xchg = None
         self.dev = current_device()
         self.lib = _lib.load()
         nx, ny = grid.nx, grid.ny
@@ -133,6 +141,33 @@ class SlabEngine:
         # Device-side plan: this rank's totals and its output bases.
         self.counts_dev = torch.zeros(len(self.isos) * 4, dtype=torch.int64, device=self.dev)
         self.bases_dev = torch.zeros(len(self.isos) * 7, dtype=torch.int64, device=self.dev)
+        if exchange == "p2p" and world > 1:
+            self._connect_p2p()
+
+    def _connect_p2p(self):
+        """Create this rank's exchange buffer and open every rank's (their
+        IPC handles travel once through the process group)."""
+        import torch.distributed as dist
+        p, lib = self.plan, self.lib
+        x = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(lib.tkmc_exchange_handle_bytes())
+        _lib.check(lib.tkmc_exchange_create(p.world, p.rank, len(self.isos), ctypes.byref(x),
+                                            handle), "tkmc_exchange_create")
+        self._xchg = x
+        handles = [None] * p.world
+        dist.all_gather_object(handles, handle.raw, group=self.group)
+        allh = ctypes.create_string_buffer(b"".join(handles))
+        _lib.check(lib.tkmc_exchange_connect(x, allh), "tkmc_exchange_connect")
+
+    def close(self):
+        """Release the exchange buffer.  Every rank calls it after its last
+        run_device (it synchronises with the other ranks first)."""
+        if self._xchg is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize(self.dev)
+            dist.barrier(group=self.group)
+            self.lib.tkmc_exchange_destroy(self._xchg)
+            self._xchg = None
 
     def count(self, local_values):
         g, p, lib = self.grid, self.plan, self.lib
@@ -169,7 +204,8 @@ class SlabEngine:
         f32 / int32 CUDA tensors whose sizes are the capacities; writes past
         them are skipped and reported by check().  When counts_host (pinned
         int64, niso*4) is given, this rank's totals are copied there
-        asynchronously.  Every rank takes the same collective each call.
+        asynchronously.  Every rank takes the same collective (or peer
+        exchange) each call.
         marks: optional 5 CUDA events, recorded before the classify, scan,
         plan and emit phases and after the emit (phase timing)."""
         import torch.distributed as dist
@@ -191,15 +227,21 @@ class SlabEngine:
         _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, p.nz_cells, ghost, niso, None,
                                     self.ws.data_ptr(), self.nbytes, st), "tkmc_fe_scan")
         mark(2)
-        _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, p.nz_cells, niso, self.ws.data_ptr(),
-                                           self.nbytes, self.counts_dev.data_ptr(), st),
-                   "tkmc_fe_copy_counts")
-        src = self.counts_dev
-        if p.world > 1:
-            dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
-            src = self.gathered
-        _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso, 0,
-                                    self.bases_dev.data_ptr(), st), "tkmc_fe_plan")
+        if self._xchg is not None:  # totals over NVLink peer stores, plan in the same kernel
+            _lib.check(lib.tkmc_exchange_plan(self._xchg, g.nx, g.ny, p.nz_cells, ghost,
+                                              self.ws.data_ptr(), self.nbytes, 0,
+                                              self.bases_dev.data_ptr(), st),
+                       "tkmc_exchange_plan")
+        else:
+            _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, p.nz_cells, niso, self.ws.data_ptr(),
+                                               self.nbytes, self.counts_dev.data_ptr(), st),
+                       "tkmc_fe_copy_counts")
+            src = self.counts_dev
+            if p.world > 1:
+                dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
+                src = self.gathered
+            _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso, 0,
+                                        self.bases_dev.data_ptr(), st), "tkmc_fe_plan")
         mark(3)
         _lib.check(lib.tkmc_fe_emit_dev(
             local_values.data_ptr(), g.nx, g.ny, p.nz_cells, ghost, p.k0,

@@ -5,7 +5,9 @@ blobs volume, runs SlabEngine (count -> one all-gather of totals -> emit)
 and sends its slices to rank 0, which assembles them and compares the result
 with a single-volume flying_edges call on its own GPU.  Each rank also
 replays the device-planned step from a CUDA graph (the NCCL all-gather of the
-totals inside it) and checks that it rewrites the same slices.  Rank 0 writes "ok"
+totals inside it), then runs it with the totals exchanged over NVLink peer
+stores (once directly, three times from a graph), and checks that every run
+rewrites the same slices.  Rank 0 writes "ok"
 to the file named by argv[1] when they are identical.
 """
 
@@ -57,6 +59,25 @@ def main():
         graph_ok = (torch.equal(pts.view(torch.int32), r["points_field"].tensor.view(torch.int32))
                     and torch.equal(conn, r["conn_field"].tensor))
         del graph
+        # The same step with the totals exchanged over NVLink peer stores.
+        eng2 = SlabEngine(grid, plan, [0.5], exchange="p2p")
+        pts.zero_()
+        eng2.run_device(vals, pts, conn)
+        torch.cuda.synchronize()
+        eng2.check()
+        graph_ok = graph_ok and torch.equal(pts.view(torch.int32),
+                                            r["points_field"].tensor.view(torch.int32))
+        graph = eng2.capture(vals, pts, conn)
+        for _ in range(3):
+            pts.zero_()
+            graph.replay()
+        torch.cuda.synchronize()
+        eng2.check()
+        graph_ok = graph_ok and torch.equal(pts.view(torch.int32),
+                                            r["points_field"].tensor.view(torch.int32)) and \
+            torch.equal(conn, r["conn_field"].tensor)
+        del graph
+        eng2.close()
         flags = [None] * world
         dist.all_gather_object(flags, graph_ok)
         parts = [None] * world
