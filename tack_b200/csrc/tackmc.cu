@@ -1026,7 +1026,6 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   __shared__ unsigned s_cnt[4][kThreads];
   __shared__ unsigned s_nu[kThreads];
   __shared__ uint32_t s_act[kThreads];
-  __shared__ long long s_red[5][kThreads / 32];
   const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
   const int32_t* __restrict__ mask_b = block_mask(ws, mask);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1094,21 +1093,19 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
     for (int t = 0; t < 4; ++t) own5[t] = s_cnt[t][tid];
     own5[4] = s_nu[tid];
   }
+  // Each warp adds its rows' totals to the tile's and the super-tile's (both
+  // zeroed before the pass): no block barrier, warps leave as they finish.
 #pragma unroll
   for (int t = 0; t < 5; ++t) {
     long long x = own5[t];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    if (lane == 0) s_red[t][warp] = x;
-  }
-  __syncthreads();
-  if (tid < 5) {
-    long long x = 0;
-#pragma unroll
-    for (int w2 = 0; w2 < kThreads / 32; ++w2) x += s_red[tid][w2];
-    Wk.agg[blockIdx.x * 5 + tid] = x;
-    atomicAdd(reinterpret_cast<unsigned long long*>(Wk.super + (blockIdx.x / kSuperTiles) * 5 + tid),
-              (unsigned long long)x);
+    if (lane == t && x != 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(Wk.agg + blockIdx.x * 5 + t),
+                (unsigned long long)x);
+      atomicAdd(reinterpret_cast<unsigned long long*>(Wk.super + (blockIdx.x / kSuperTiles) * 5 + t),
+                (unsigned long long)x);
+    }
   }
 }
 
@@ -2876,7 +2873,7 @@ struct FeLayout {
   int64_t super_stride;
   size_t off_bits, off_sums, off_cnt, off_wact, off_tot, off_base, off_rowoff, off_work, off_info, off_flags,
       off_agg, off_incl, total;
-  size_t reset_bytes;  // info + flags, zeroed before each scan
+  size_t reset_bytes;  // end of the per-call state zeroed before each count
 };
 
 bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout* out) {
@@ -2929,8 +2926,8 @@ bool fe_layout(int64_t nx, int64_t ny, int64_t nz, int ghost, int niso, FeLayout
   f.off_flags = o;  o = align_up(o + (size_t)niso * d.ntiles * 4, 256);
   f.super_stride = aligned ? (d.ntiles + kSuperTiles - 1) / kSuperTiles * 5 : 0;
   f.off_super = o;  o = align_up(o + (size_t)niso * f.super_stride * 8, 256);
-  f.reset_bytes = o;
   f.off_agg = o;    o = align_up(o + (size_t)niso * d.ntiles * 5 * 8, 256);
+  f.reset_bytes = o;  // info, flags, super-tile and tile totals start at zero
   f.off_incl = o;   o = align_up(o + (size_t)niso * d.ntiles * 5 * 8, 256);
   f.off_tot = o;    o = align_up(o + (size_t)niso * 4 * 8, 256);
   f.off_base = o;   o = align_up(o + (size_t)niso * 8 * 8, 256);
