@@ -93,18 +93,63 @@ def committed_traffic():
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during a region."""
+    """SM clock, power and clock-event reasons of this rank's GPU, read through
+    NVML (reads only) by a thread every ~2 ms while the timed steps run, plus
+    one sample taken by the caller while queued steps are still executing
+    (``sample_now``), so a short timed region still has a sample under load.
+    Falls back to ``nvidia-smi -lms`` when NVML cannot be opened."""
 
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device_index):
         self.dev = device_index
-        self.proc = None
-        self.path = None
+        self.nvml = self.handle = None
+        self.rows = []          # (sm_mhz, max_mhz, power_w, reason bits)
+        self.thread = self.halt = None
+        self.proc = self.path = None
+
+    def _open_nvml(self):
+        import torch
+        import pynvml
+        pynvml.nvmlInit()
+        pr = torch.cuda.get_device_properties(self.dev)
+        bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        self.nvml = pynvml
+
+    def sample_now(self):
+        if self.nvml is None:
+            return
+        n, h = self.nvml, self.handle
+        try:
+            get_reasons = getattr(n, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                n.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.rows.append((n.nvmlDeviceGetClockInfo(h, n.NVML_CLOCK_SM),
+                              n.nvmlDeviceGetMaxClockInfo(h, n.NVML_CLOCK_SM),
+                              n.nvmlDeviceGetPowerUsage(h) / 1000.0, int(get_reasons(h))))
+        except Exception:
+            pass
 
     def start(self):
+        import threading
+        try:
+            self._open_nvml()
+        except Exception:
+            self.nvml = None
+        if self.nvml is not None:
+            self.halt = threading.Event()
+
+            def loop():
+                while not self.halt.is_set():
+                    self.sample_now()
+                    self.halt.wait(0.002)
+            self.thread = threading.Thread(target=loop, daemon=True)
+            self.thread.start()
+            return
         import tempfile
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
@@ -117,8 +162,23 @@ class ClockSampler:
             self.proc = None
 
     def stop(self):
+        if self.thread is not None:
+            self.halt.set()
+            self.thread.join(timeout=5)
+            rows = self.rows
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
+            if not rows:
+                return {"samples": 0, "source": "nvml"}
+            return {"sm_mhz": statistics.median(r[0] for r in rows),
+                    "sm_max_mhz": max(r[1] for r in rows),
+                    "power_w": round(statistics.median(r[2] for r in rows), 1),
+                    "reasons": sorted({nm for r in rows for nm, bit in self.REASONS if r[3] & bit}),
+                    "samples": len(rows), "source": "nvml"}
         if self.proc is None:
-            return {"samples": 0, "note": "nvidia-smi unavailable"}
+            return {"samples": 0, "note": "neither NVML nor nvidia-smi available"}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -131,14 +191,14 @@ class ClockSampler:
                 rows.append(parts)
         os.unlink(self.path)
         if not rows:
-            return {"samples": 0}
+            return {"samples": 0, "source": "nvidia-smi"}
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [nm for nm, _ in self.REASONS]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------- reference arm
@@ -324,6 +384,7 @@ def main():
     for i in range(K):
         graph.replay()
     t_end.record(stream)
+    clocks.sample_now()  # the queued steps are still running
     torch.cuda.synchronize()
     launches = per_step * K
     eng.check()  # any device-recorded error (capacity, timeout) invalidates the run
