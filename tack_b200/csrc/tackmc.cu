@@ -2533,9 +2533,13 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
   __syncwarp();
   const unsigned long long ep = s_epoch;
   // This rank's totals {X, Y, Z, T} per isovalue (info[16 q + 0..3]) into
-  // slot `rank` of every rank's gathered array.
+  // slot `rank` of every rank's gathered array.  The array has two halves,
+  // used by odd and even epochs: a rank that finished waiting in epoch e may
+  // still be reading half e % 2 when a faster peer writes epoch e + 1, and no
+  // peer can reach epoch e + 2 before this rank has published e + 1.
+  const int64_t half = (int64_t)(ep & 1ull) * world * niso * 4;
   for (int r = lane; r < world; r += 32) {
-    long long* dst = peers.gathered[r] + (int64_t)rank * niso * 4;
+    long long* dst = peers.gathered[r] + half + (int64_t)rank * niso * 4;
     for (int q = 0; q < niso; ++q)
       for (int t = 0; t < 4; ++t) dst[4 * q + t] = own_info[16 * q + t];
   }
@@ -2560,7 +2564,7 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
     atomicExch((unsigned long long*)err, (unsigned long long)TKMC_ERR_DEVICE_TIMEOUT);
   __syncwarp();
   if (lane == 0)
-    k_fe_plan_body(peers.gathered[rank], world, rank, niso, shared_output, bases);
+    k_fe_plan_body(peers.gathered[rank] + half, world, rank, niso, shared_output, bases);
 }
 
 
@@ -3642,7 +3646,7 @@ int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx, in
 
 struct tkmc_exchange_impl {
   int world, rank, niso, device;
-  char* base;  // one allocation: flags [world] u64 | gathered [world][niso][4] i64 | epoch u64
+  char* base;  // one allocation: flags [world] u64 | gathered [2][world][niso][4] i64 | epoch u64
   size_t off_gathered, off_epoch, bytes;
   ExchangePeers peers;
   void* opened[kMaxRanks];
@@ -3661,7 +3665,7 @@ int tkmc_exchange_create(int world, int rank, int niso, void** out, void* handle
   x->niso = niso;
   cudaError_t e = cudaGetDevice(&x->device);
   x->off_gathered = align_up((size_t)world * 8, 256);
-  x->off_epoch = x->off_gathered + align_up((size_t)world * niso * 4 * 8, 256);
+  x->off_epoch = x->off_gathered + align_up((size_t)2 * world * niso * 4 * 8, 256);
   x->bytes = x->off_epoch + 256;
   if (e == cudaSuccess) e = cudaMalloc(&x->base, x->bytes);
   if (e == cudaSuccess) e = cudaMemset(x->base, 0, x->bytes);

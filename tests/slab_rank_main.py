@@ -6,9 +6,10 @@ and sends its slices to rank 0, which assembles them and compares the result
 with a single-volume flying_edges call on its own GPU.  Each rank also
 replays the device-planned step from a CUDA graph (the NCCL all-gather of the
 totals inside it), then runs it with the totals exchanged over NVLink peer
-stores (once directly, three times from a graph), and checks that every run
-rewrites the same slices.  Rank 0 writes "ok"
-to the file named by argv[1] when they are identical.
+stores (once directly, three times from a graph, then four steps alternating
+between two different volumes), and checks that every run writes that
+volume's slices.  Rank 0 writes "ok" to the file named by argv[1] when they
+are identical.
 """
 
 import os
@@ -77,6 +78,23 @@ def main():
                                             r["points_field"].tensor.view(torch.int32)) and \
             torch.equal(conn, r["conn_field"].tensor)
         del graph
+        # Steps over two different volumes in turn: every exchange carries
+        # new totals, and each step's slices must match that volume's
+        # host-planned run.
+        vals_b = (vals * 1.25).contiguous()
+        rb = eng.run(vals_b)
+        pts_b = torch.zeros_like(rb["points_field"].tensor)
+        conn_b = torch.zeros_like(rb["conn_field"].tensor)
+        for i in range(4):
+            src, p_out, c_out, ref_r = ((vals, pts, conn, r) if i % 2 == 0
+                                        else (vals_b, pts_b, conn_b, rb))
+            p_out.zero_()
+            eng2.run_device(src, p_out, c_out)
+            torch.cuda.synchronize()
+            eng2.check()
+            graph_ok = graph_ok and torch.equal(
+                p_out.view(torch.int32), ref_r["points_field"].tensor.view(torch.int32)) and \
+                torch.equal(c_out, ref_r["conn_field"].tensor)
         eng2.close()
         flags = [None] * world
         dist.all_gather_object(flags, graph_ok)
