@@ -25,8 +25,9 @@ def stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def capi_fe(values, grid, isovalues, mask=None, want_rows=False):
-    """Count + emit through the C ABI; returns dict of host arrays.
+def capi_fe(values, grid, isovalues, mask=None, want_rows=False, host=True):
+    """Count + emit through the C ABI; returns dict of host arrays (points
+    and conn stay CUDA tensors, shaped (-1, 3), when host is False).
 
     values: flat f32 CUDA tensor or numpy array.  grid: (nx, ny, nz, x0, y0,
     z0, dx, dy, dz).  isovalues: list (<= 8).
@@ -72,6 +73,10 @@ def capi_fe(values, grid, isovalues, mask=None, want_rows=False):
     _lib.check(lib.tkmc_fe_check(nx, ny, nz, niso, ws.data_ptr(), nbytes, stream()),
                "tkmc_fe_check")
     torch.cuda.synchronize()
+    if not host:
+        return {"counts": counts.reshape(niso, 4), "points": pts[:P * 3].view(-1, 3),
+                "conn": conn[:T * 3].view(-1, 3), "rows": rows, "total_points": P,
+                "total_tris": T}
     return {"counts": counts.reshape(niso, 4), "points": pts[:P * 3].cpu().numpy().reshape(-1, 3),
             "conn": conn[:T * 3].cpu().numpy().reshape(-1, 3), "rows": rows,
             "total_points": P, "total_tris": T}
