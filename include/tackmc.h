@@ -278,6 +278,13 @@ int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx,
 size_t tkmc_exchange_handle_bytes(void);
 int tkmc_exchange_create(int world, int rank, int niso, void** exchange, void* handle);
 int tkmc_exchange_connect(void* exchange, const void* handles);
+/* Connect without IPC: `members` are all ranks' exchanges (rank order, this
+ * one included), created in this process on this device.  For emulating the
+ * group in one process: kernels that wait on one another must not run as
+ * separate launches on one GPU, so only one member may call
+ * tkmc_exchange_plan -- its wait then ends by the time limit
+ * (tkmc_set_wait_limit_ns) with TKMC_ERR_DEVICE_TIMEOUT. */
+int tkmc_exchange_connect_local(void* exchange, void* const* members);
 int tkmc_exchange_plan(void* exchange, int64_t nx, int64_t ny, int64_t nz,
                        int ghost_plane, const void* workspace, size_t workspace_bytes,
                        int shared_output, int64_t* bases_dev, void* stream);

@@ -51,6 +51,7 @@ SIGNATURES = {
     "tkmc_exchange_handle_bytes": (_SZ, []),
     "tkmc_exchange_create": (_I, [_I, _I, _I, _P, _P]),
     "tkmc_exchange_connect": (_I, [_P, _P]),
+    "tkmc_exchange_connect_local": (_I, [_P, _P]),
     "tkmc_exchange_plan": (_I, [_P, _I64, _I64, _I64, _I, _P, _SZ, _I, _P, _P]),
     "tkmc_exchange_destroy": (_I, [_P]),
     "tkmc_fe_emit_soup": (_I, [_P, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P,

@@ -3376,7 +3376,7 @@ int tkmc_fe_check(int64_t nx, int64_t ny, int64_t nz, int niso, void* ws, size_t
   for (int q = 0; q < niso; ++q) {
     const long long e = h[q * 16 + 10];
     if (e == TKMC_ERR_DEVICE_TIMEOUT)
-      return set_err((int)e, "fe scan look-back wait expired (isovalue %d)", q);
+      return set_err((int)e, "a device wait expired: scan look-back or totals exchange (isovalue %d)", q);
     if (e)
       return set_err((int)e, "fe emit wrote past the output capacity (isovalue %d)", q);
   }
@@ -3695,6 +3695,20 @@ int tkmc_exchange_connect(void* xp, const void* handles) {
     }
     x->peers.flags[r] = reinterpret_cast<unsigned long long*>(b);
     x->peers.gathered[r] = reinterpret_cast<long long*>(b + x->off_gathered);
+  }
+  return TKMC_OK;
+}
+
+int tkmc_exchange_connect_local(void* xp, void* const* members) {
+  tkmc_exchange_impl* x = static_cast<tkmc_exchange_impl*>(xp);
+  if (!x || !members)
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_connect_local: NULL argument");
+  for (int r = 0; r < x->world; ++r) {
+    const tkmc_exchange_impl* m = static_cast<const tkmc_exchange_impl*>(members[r]);
+    if (!m || m->world != x->world || m->rank != r || m->niso != x->niso || m->device != x->device)
+      return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_connect_local: member %d does not match", r);
+    x->peers.flags[r] = reinterpret_cast<unsigned long long*>(m->base);
+    x->peers.gathered[r] = reinterpret_cast<long long*>(m->base + m->off_gathered);
   }
   return TKMC_OK;
 }

@@ -63,3 +63,42 @@ def test_scan_wait_expires_with_status(tack, short_wait):
     assert rc == 0 and tot.value == n
     assert torch.equal(out.cpu(), torch.arange(n, dtype=torch.int32))
 
+
+
+def test_exchange_wait_expires_with_status(tack, short_wait):
+    """A peer that never runs its totals exchange: rank 0's wait for the
+    peer's flag (a flag nothing sets) ends by the time limit, the status is
+    read back by tkmc_fe_check, and the context stays usable.  Both ranks'
+    exchanges live in this process; only rank 0 launches."""
+    import ctypes
+    lib = short_wait
+    c = load_fe_case("gyroid48")
+    nx, ny, nz = c["grid_tuple"][:3]
+    v = torch.from_numpy(c["values"]).cuda()
+    nb = lib.tkmc_fe_workspace_bytes(nx, ny, nz, 1)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    counts = np.zeros(4, np.int64)
+    assert lib.tkmc_fe_count(v.data_ptr(), nx, ny, nz, 0, f32arr([0.0]), 1, None, ws.data_ptr(),
+                             nb, counts.ctypes.data, stream()) == 0
+    hb = lib.tkmc_exchange_handle_bytes()
+    ex = [ctypes.c_void_p(), ctypes.c_void_p()]
+    handles = [ctypes.create_string_buffer(hb) for _ in ex]
+    for r in range(2):
+        assert lib.tkmc_exchange_create(2, r, 1, ctypes.byref(ex[r]), handles[r]) == 0
+    try:
+        members = (ctypes.c_void_p * 2)(ex[0].value, ex[1].value)
+        assert lib.tkmc_exchange_connect_local(ex[0], members) == 0
+        bad = (ctypes.c_void_p * 2)(ex[1].value, ex[0].value)  # wrong rank order
+        assert lib.tkmc_exchange_connect_local(ex[0], bad) == _lib.TKMC_ERR_INVALID_ARG
+        bases = torch.zeros(7, dtype=torch.int64, device="cuda")
+        assert lib.tkmc_exchange_plan(ex[0], nx, ny, nz, 0, ws.data_ptr(), nb, 0,
+                                      bases.data_ptr(), stream()) == 0
+        rc = lib.tkmc_fe_check(nx, ny, nz, 1, ws.data_ptr(), nb, stream())
+        assert rc == _lib.TKMC_ERR_DEVICE_TIMEOUT
+        assert b"wait expired" in lib.tkmc_last_error()
+    finally:
+        torch.cuda.synchronize()
+        for x in ex:
+            lib.tkmc_exchange_destroy(x)
+    got = capi_fe(c["values"], c["grid_tuple"], [0.0])
+    np.testing.assert_array_equal(got["conn"], c["conn"])
