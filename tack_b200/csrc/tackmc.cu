@@ -359,12 +359,47 @@ k_fe_threshold_v4(const float* __restrict__ v, int64_t nfull, IsoParams iso, int
   }
 }
 
+template <int NISO>
+__device__ __forceinline__ void threshold_multi_body(const float* __restrict__ p, const IsoParams& iso,
+                                                     uint32_t* __restrict__ bits, int64_t bits_stride,
+                                                     uint2* __restrict__ sums, int64_t sums_stride,
+                                                     int64_t ch, int lane) {
+  float th[NISO];
+  uint32_t word[NISO];
+#pragma unroll
+  for (int t = 0; t < NISO; ++t) {
+    th[t] = iso.v[t];
+    word[t] = 0u;
+  }
+  float x[32];
+#pragma unroll
+  for (int q = 0; q < 32; ++q) x[q] = __ldcs(p + 32 * q);
+#pragma unroll
+  for (int q = 0; q < 32; ++q) {
+    const bool mine = lane == q;
+#pragma unroll
+    for (int t = 0; t < NISO; ++t) {
+      const uint32_t b = __ballot_sync(0xffffffffu, x[q] > th[t]);
+      word[t] = mine ? b : word[t];
+    }
+  }
+  const int64_t wi = (ch << 5) + lane;
+#pragma unroll
+  for (int t = 0; t < NISO; ++t) {
+    bits[t * bits_stride + wi] = word[t];
+    store_summary(sums + t * sums_stride, ch, word[t], lane);
+  }
+}
+
 // Several isovalues: lane l loads nodes l, 32 + l, ..., 992 + l of the chunk
 // (32 coalesced 128-byte loads per warp), so that each ballot is directly
 // the bit word of 32 consecutive nodes and no interleave is needed -- per
 // isovalue 32 compares, 32 ballots and 32 selects instead of the float4
 // layout's ballots plus four-way interleave, which leaves the kernel issue
-// bound once it runs for several isovalues.  Full chunks only, like v4.
+// bound once it runs for several isovalues.  The isovalue count is a
+// template parameter, so the isovalues' ballot chains of one node column
+// interleave (independent work for the scheduler) and share the lane test.
+// Full chunks only, like v4.
 __global__ void __launch_bounds__(kThreads, 5)
 k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
                      uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
@@ -384,20 +419,16 @@ k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, 
   }
   if (ch >= nfull) return;  // whole warps only
   const float* __restrict__ p = v + (ch << 10) + lane;
-  float x[32];
-#pragma unroll
-  for (int q = 0; q < 32; ++q) x[q] = __ldcs(p + 32 * q);
-  const int64_t wi = (ch << 5) + lane;
-  for (int t = 0; t < niso; ++t) {
-    const float th = iso.v[t];
-    uint32_t word = 0;
-#pragma unroll
-    for (int q = 0; q < 32; ++q) {
-      const uint32_t b = __ballot_sync(0xffffffffu, x[q] > th);
-      word = lane == q ? b : word;
-    }
-    bits[t * bits_stride + wi] = word;
-    store_summary(sums + t * sums_stride, ch, word, lane);
+  switch (niso) {  // 1 <= niso <= TKMC_MAX_ISO, checked by the host
+    case 1: threshold_multi_body<1>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 2: threshold_multi_body<2>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 3: threshold_multi_body<3>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 4: threshold_multi_body<4>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 5: threshold_multi_body<5>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 6: threshold_multi_body<6>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 7: threshold_multi_body<7>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    case 8: threshold_multi_body<8>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+    default: break;
   }
 }
 
