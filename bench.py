@@ -45,6 +45,10 @@ if REPO not in sys.path:
 
 METRIC = "isosurface input Gcells/s at 1/2/4/8 B200; achieved HBM GB/s vs peak"
 TRAFFIC_FILE = os.path.join(REPO, "profiles", "fe_threshold_blobs1024.txt")
+# Relative device time per node (threshold read, 4 B at ~6.5 TB/s: 0.6 ps) and
+# per triangle (count + emit: 0.27 ms for 5.3 M triangles, 51 ps) on one
+# B200 at 1024^3 blobs; used to balance z-slabs at N > 1.
+NODE_COST, TRI_COST = 1.0, 83.0
 
 
 def parse_args():
@@ -62,6 +66,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="totals exchange between ranks (N>1): NVLink peer stores or NCCL")
+    ap.add_argument("--balance-slabs", action="store_true",
+                    help="N>1: node-plane runs balanced by the surface of a first pass "
+                         "instead of equal runs")
     return ap.parse_args()
 
 
@@ -302,7 +309,7 @@ def main():
 
     import tack_b200 as tack
     from tack_b200 import _lib, workloads
-    from tack_b200.distributed import SlabEngine, SlabPlan, slab_bases
+    from tack_b200.distributed import SlabEngine, SlabPlan, balanced_bounds, slab_bases
 
     rank, world, local = dist_env()
     if world != args.gpus:
@@ -333,6 +340,28 @@ def main():
     # (the totals reach the host asynchronously, as a caller would read them).
     first = eng.run(vol)
     own = first["counts"]
+    balanced = None
+    if world > 1 and args.balance_slabs:
+        # Slab bounds balanced by predicted device time: the surface of this
+        # first pass (in a time series, the previous step's) gives each node
+        # plane's triangles; a plane costs NODE_COST per node (the threshold
+        # read) plus TRI_COST per triangle (count and emit).  Then the slabs
+        # are set up again on the new bounds.
+        tris = eng.plane_triangles(own)
+        allt = [None] * world
+        dist.all_gather_object(allt, tris.tolist())
+        plane_tris = np.concatenate([np.asarray(t, np.float64) for t in allt])
+        work = NODE_COST * nxn * nyn + TRI_COST * plane_tris
+        balanced = balanced_bounds(work, world)
+        eng.close()
+        del eng, vol, first
+        plan = SlabPlan(nzn, world, rank, bounds=balanced)
+        vol = workloads.generate(args.config, shape, plan.k0, plan.k1, device=dev)
+        torch.cuda.synchronize()
+        eng = SlabEngine(grid, plan, isos, exchange=args.exchange)
+        local_nodes = vol.numel()
+        first = eng.run(vol)
+        own = first["counts"]
     own_p, own_t = int(own[:, :3].sum()), int(own[:, 3].sum())
     pts_buf = torch.empty(max(own_p, 1) * 3, dtype=torch.float32, device=dev)
     conn_buf = torch.empty(max(own_t, 1) * 3, dtype=torch.int32, device=dev)
@@ -394,6 +423,15 @@ def main():
     barrier()
     ms = t_start.elapsed_time(t_end)
     del graph
+    # The threshold kernel's roofline at N > 1: the rank with the lowest
+    # achieved bandwidth (slabs can differ in size), with its own bytes.
+    k1_rank = torch.tensor([4.0 * local_nodes / (k1 * 1e-3), float(local_nodes), k1],
+                           dtype=torch.float64, device=dev)
+    if world > 1:
+        allk1 = [torch.zeros_like(k1_rank) for _ in range(world)]
+        dist.all_gather(allk1, k1_rank)
+        k1_rank = min(allk1, key=lambda t: float(t[0]))
+    k1_nodes, k1_ms = float(k1_rank[1]), float(k1_rank[2])
     stats = torch.tensor([ms, k1, k2, k3, host], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
@@ -434,11 +472,11 @@ def main():
         dist.barrier()
     if rank == 0:
         peak, peak_src = measured_peaks()
-        alg_k1 = 4.0 * local_nodes  # one read of this rank's slab (incl. ghost)
-        achieved = alg_k1 / (k1 * 1e-3) / 1e9
+        alg_k1 = 4.0 * k1_nodes  # one read of that rank's slab (incl. ghost)
+        achieved = alg_k1 / (k1_ms * 1e-3) / 1e9
         traffic = committed_traffic()
         if traffic is not None:
-            traffic = traffic * local_nodes / float(1024 ** 3)
+            traffic = traffic * k1_nodes / float(1024 ** 3)
         step_bytes = 4.0 * nxn * nyn * nzn + 12.0 * (total_points + total_tris)
         value = cells * K / (ms * 1e-3) / 1e9
         out = {
@@ -450,8 +488,10 @@ def main():
                 "workload": workload_name(args.config, shape, isos),
                 "volume_nodes": list(shape), "cells": cells, "isovalues": isos,
                 "parallelism": (f"z-slab x{world} (ghost plane; totals exchanged by "
-                                f"{'NVLink peer stores' if args.exchange == 'p2p' else 'NCCL all-gather'})"
+                                f"{'NVLink peer stores' if args.exchange == 'p2p' else 'NCCL all-gather'}; "
+                                f"{'equal plane runs' if balanced is None else 'plane runs balanced by surface'})"
                                 if world > 1 else "single GPU"),
+                "slab_bounds": balanced,
                 "l2": (f"inputs larger than L2 (f32 slab {4.0 * local_nodes / 2**30:.2f} GiB per "
                        f"GPU vs 126 MB L2), no flush" if 4.0 * local_nodes > 126e6 * 2 else
                        "input smaller than 2x L2: numbers include L2 reuse between steps"),
@@ -461,7 +501,7 @@ def main():
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": traffic, "peak_source": peak_src,
                 "algorithmic_bytes_per_launch": alg_k1,
-                "launch_ms": k1,
+                "launch_ms": k1_ms,
             },
             "step_roofline": {
                 "algorithmic_bytes": step_bytes,

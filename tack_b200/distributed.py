@@ -29,15 +29,24 @@ from .runtime import current_device, current_stream
 
 
 class SlabPlan:
-    """Node-plane ownership of `rank` among `world` for nz_nodes planes."""
+    """Node-plane ownership of `rank` among `world` for nz_nodes planes:
+    equal runs, or the runs [bounds[r], bounds[r + 1]) when `bounds` (world + 1
+    increasing plane indices from 0 to nz_nodes) is given."""
 
-    def __init__(self, nz_nodes, world, rank):
+    def __init__(self, nz_nodes, world, rank, bounds=None):
         if not (0 <= rank < world) or nz_nodes < 2 * world:
             raise ValueError(f"cannot split {nz_nodes} planes over {world} ranks")
-        base, rem = divmod(nz_nodes, world)
         self.rank, self.world, self.nz_nodes = rank, world, nz_nodes
-        self.p0 = rank * base + min(rank, rem)
-        self.p1 = self.p0 + base + (1 if rank < rem else 0)
+        if bounds is None:
+            base, rem = divmod(nz_nodes, world)
+            self.p0 = rank * base + min(rank, rem)
+            self.p1 = self.p0 + base + (1 if rank < rem else 0)
+        else:
+            b = [int(x) for x in bounds]
+            if (len(b) != world + 1 or b[0] != 0 or b[-1] != nz_nodes or
+                    any(b[i + 1] - b[i] < 1 for i in range(world)) or b[-1] - b[-2] < 2):
+                raise ValueError(f"bad slab bounds {b} for {nz_nodes} planes, {world} ranks")
+            self.p0, self.p1 = b[rank], b[rank + 1]
         self.ghost = self.p1 < nz_nodes
         self.k0 = self.p0                      # first local plane
         self.k1 = min(self.p1 + 1, nz_nodes)   # one past the last local plane
@@ -50,6 +59,30 @@ class SlabPlan:
     def __repr__(self):
         return (f"SlabPlan(rank={self.rank}/{self.world}, own=[{self.p0},{self.p1}), "
                 f"local=[{self.k0},{self.k1}), ghost={self.ghost})")
+
+
+def balanced_bounds(work, world, min_planes=2):
+    """Slab bounds for SlabPlan: `world` contiguous runs of node planes whose
+    sums of per-plane `work` are as equal as the plane granularity allows
+    (each run at least `min_planes` planes).  A plane's work is whatever
+    predicts its device time, e.g. a cost per node plus a cost per triangle
+    of the cell layer above it (from an earlier count of the same or a
+    previous volume)."""
+    w = np.asarray(work, np.float64)
+    n = w.size
+    if world < 1 or n < min_planes * world:
+        raise ValueError(f"cannot split {n} planes over {world} ranks")
+    c = np.concatenate([[0.0], np.cumsum(w)])
+    bounds = [0]
+    for r in range(1, world):
+        target = c[-1] * r / world
+        k = int(np.searchsorted(c, target))
+        if k > 0 and (k > n or abs(c[k - 1] - target) <= abs(c[k] - target)):
+            k -= 1
+        k = min(max(k, bounds[-1] + min_planes), n - (world - r) * min_planes)
+        bounds.append(k)
+    bounds.append(n)
+    return bounds
 
 
 def slab_bases(all_counts, rank):
@@ -178,6 +211,25 @@ class SlabEngine:
                                      self.ws.data_ptr(), self.nbytes, counts.ctypes.data,
                                      current_stream(self.dev)), "tkmc_fe_count")
         return counts.reshape(niso, 4)
+
+    def plane_triangles(self, counts):
+        """Triangles of the cell layer above each own node plane (all
+        isovalues), from the last count on this engine; counts is that
+        count's [niso, 4] totals.  Copies the row table to the host
+        (synchronises)."""
+        g, p, lib = self.grid, self.plan, self.lib
+        niso = len(self.isos)
+        rows = (g.ny + 1) * (p.nz_cells + 1)
+        own = p.p1 - p.p0
+        out = np.zeros(rows * 4, np.int64)
+        tris = np.zeros(own, np.int64)
+        for q in range(niso):
+            _lib.check(lib.tkmc_fe_row_offsets(g.nx, g.ny, p.nz_cells, niso, q, self.ws.data_ptr(),
+                                               self.nbytes, out.ctypes.data,
+                                               current_stream(self.dev)), "tkmc_fe_row_offsets")
+            per_row = np.diff(np.append(out.reshape(rows, 4)[:, 3], int(counts[q, 3])))
+            tris += per_row.reshape(p.nz_cells + 1, g.ny + 1)[:own].sum(axis=1)
+        return tris
 
     def exchange(self, counts):
         """All-gather every rank's totals (one collective)."""

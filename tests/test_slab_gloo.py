@@ -16,7 +16,7 @@ from datetime import timedelta
 import numpy as np
 import pytest
 
-from tack_b200.distributed import SlabPlan, assemble, gather_counts, slab_bases
+from tack_b200.distributed import SlabPlan, assemble, balanced_bounds, gather_counts, slab_bases
 
 SHAPE = (23, 17, 29)          # cells; node planes along z: 30
 
@@ -111,6 +111,48 @@ def test_plans_partition_the_planes():
         SlabPlan(3, 2, 0)
     with pytest.raises(ValueError):
         SlabPlan(30, 2, 2)
+
+
+def test_balanced_bounds():
+    """Equal work gives equal runs; a dense band gets short runs; every run
+    keeps at least two planes; the bounds partition the planes."""
+    assert balanced_bounds(np.ones(1024), 8) == [128 * r for r in range(9)]
+    w = np.ones(1024)
+    w[400:600] += 50.0
+    b = balanced_bounds(w, 8)
+    sums = [w[b[i]:b[i + 1]].sum() for i in range(8)]
+    assert max(sums) - min(sums) <= 2 * w.max()
+    assert b[1] > 300 and b[-2] < 700
+    assert balanced_bounds(np.ones(16), 8) == list(range(0, 17, 2))
+    spike = np.zeros(40)
+    spike[5] = 1e6
+    b = balanced_bounds(spike, 4)
+    assert b[0] == 0 and b[-1] == 40 and all(b[i + 1] - b[i] >= 2 for i in range(4))
+    with pytest.raises(ValueError):
+        balanced_bounds(np.ones(7), 4)
+
+
+@pytest.mark.parametrize("world", [2, 3, 5])
+def test_uneven_slabs_assemble_to_single_volume(oracle, world):
+    """Slabs on surface-balanced bounds (uneven runs) assemble to the
+    single-volume output, like equal runs."""
+    vol = _volume()
+    isos = [0.0, 1.5, -3.0]
+    nzn = SHAPE[2] + 1
+    w = np.arange(nzn, dtype=np.float64) ** 2 + 1.0
+    bounds = balanced_bounds(w, world)
+    plans = [SlabPlan(nzn, world, r, bounds=bounds) for r in range(world)]
+    assert [p.p0 for p in plans] + [plans[-1].p1] == bounds
+    per = [_rank_counts(oracle, vol, p, isos) for p in plans]
+    allc = np.stack([c for c, _, _, _ in per])
+    parts = []
+    for p, (counts, infos, local, g) in zip(plans, per):
+        parts.append(_rank_emit(oracle, local, g, isos, infos, counts, slab_bases(allc, p.rank)))
+    _check(parts, _reference(oracle, vol, isos))
+    with pytest.raises(ValueError):
+        SlabPlan(nzn, world, 0, bounds=bounds[:-1])
+    with pytest.raises(ValueError):
+        SlabPlan(nzn, 2, 0, bounds=[0, nzn - 1, nzn])
 
 
 def test_slab_bases_known_answer():

@@ -23,11 +23,11 @@ pytestmark = pytest.mark.gpu
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-def _run_slabs_one_gpu(tack, vol_dev, grid, isos, world):
+def _run_slabs_one_gpu(tack, vol_dev, grid, isos, world, bounds=None):
     from tack_b200.distributed import SlabEngine, SlabPlan, assemble, slab_bases
     nx, ny, nz = grid.nx, grid.ny, grid.nz
     plane = (nx + 1) * (ny + 1)
-    plans = [SlabPlan(nz + 1, world, r) for r in range(world)]
+    plans = [SlabPlan(nz + 1, world, r, bounds=bounds) for r in range(world)]
     engines, counts, locals_ = [], [], []
     for p in plans:
         eng = SlabEngine(grid, p, isos)
@@ -61,6 +61,37 @@ def test_slabs_match_single_volume_oracle(tack, oracle, shape, world):
     ref = oracle.flying_edges_isovalues(v, oracle.Grid(*g), isos)
     np.testing.assert_array_equal(conn, ref["conn"])
     assert_points_identical(points, ref["points"])
+
+
+def test_surface_balanced_slabs_match_single_volume(tack):
+    """Slab bounds from the surface of a first pass (per-plane triangles from
+    each equal slab's row table, a cost per node and per triangle): the
+    slabs are uneven, and the sharded surface still equals the single-volume
+    surface."""
+    from tack_b200 import workloads
+    from tack_b200.distributed import SlabEngine, SlabPlan, balanced_bounds
+    shape = (128, 128, 128)
+    whole = workloads.generate("blobs", shape)
+    nx, ny, nz = shape[0] - 1, shape[1] - 1, shape[2] - 1
+    grid = tack.UniformGrid(nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+    plane = shape[0] * shape[1]
+    world = 4
+    per_plane = []
+    for r in range(world):
+        p = SlabPlan(shape[2], world, r)
+        eng = SlabEngine(grid, p, [0.5])
+        local = whole[p.k0 * plane:p.k1 * plane]
+        c = eng.count(local)
+        per_plane.append(eng.plane_triangles(c))
+    tris = np.concatenate(per_plane)
+    assert tris.size == shape[2] and int(tris.sum()) > 0
+    r = tack.flying_edges(tack.from_torch(whole), grid, 0.5)
+    assert int(tris.sum()) == r["total_tris"]
+    bounds = balanced_bounds(plane + 83.0 * tris, world)
+    assert bounds != [0, 32, 64, 96, 128]
+    points, conn = _run_slabs_one_gpu(tack, whole, grid, [0.5], world, bounds=bounds)
+    np.testing.assert_array_equal(conn, r["conn"])
+    assert_points_identical(points, r["points"])
 
 
 def test_slabs_blobs_256_match_single_volume(tack):
