@@ -1468,12 +1468,12 @@ __device__ __forceinline__ unsigned seg_scan(unsigned x, int sl, int S) {
 //   8     cells with triangles (before the mask)
 //   9-16  bit words a a1 b b1 c c1 d d1 (x1 = next node)
 //   17-32 int64 id offset of each group's first crossing in this word (lo, hi)
-//   33-34 int64 triangle offset of the row
+//   33-34 (unused)
 //   35-36 j, k of the row
 //   37-38 exclusive prefix over the warp's words of points / active cells
 constexpr int kRec = 39;
-constexpr int kRecMasks = 0, kRecAct = 8, kRecBits = 9, kRecOff = 17, kRecTri = 33, kRecJ = 35,
-              kRecK = 36, kRecPB = 37, kRecCB = 38;
+constexpr int kRecMasks = 0, kRecAct = 8, kRecBits = 9, kRecOff = 17, kRecJ = 35, kRecK = 36,
+              kRecPB = 37, kRecCB = 38;
 
 
 __device__ __forceinline__ long long rec_i64(const uint32_t* rec, int at) {
