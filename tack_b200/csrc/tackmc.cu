@@ -195,15 +195,6 @@ __device__ __forceinline__ float interp_t(float iso, float s, float s1) {
   return __fdiv_rn(__fsub_rn(iso, s), __fadd_rn(__fsub_rn(s1, s), 1.0e-10f));
 }
 
-// 8 bits -> bit positions 0, 4, 8, ..., 28.
-__device__ __forceinline__ uint32_t spread8(uint32_t x) {
-  x &= 0xffu;
-  x = (x | (x << 12)) & 0x000f000fu;
-  x = (x | (x << 6)) & 0x03030303u;
-  x = (x | (x << 3)) & 0x11111111u;
-  return x;
-}
-
 // ------------------------------------------------------------------------
 // decoupled look-back (single-pass scan across tiles)
 // ------------------------------------------------------------------------
@@ -298,10 +289,15 @@ __device__ void lookback(uint32_t* flags, long long* agg, long long* incl,
 // K1: threshold the volume into node bitmasks (all isovalues, one read)
 // ------------------------------------------------------------------------
 //
-// A warp takes 1024 consecutive nodes (4 KiB): eight coalesced 512-byte
-// float4 loads, issued before any use.  Four ballots per load give
-// the "above" bits in lane-interleaved order; each lane assembles one 32-bit
-// word of node order and the warp stores 32 words (128 B) coalesced.
+// A warp takes 1024 consecutive nodes (4 KiB): lane l loads nodes l, 32 + l,
+// ..., 992 + l (32 coalesced 128-byte loads, all issued before any use), so
+// each ballot over the warp is directly the bit word of 32 consecutive nodes
+// and lane q keeps ballot q: per isovalue 32 compares, 32 ballots and 32
+// selects, no interleave.  The warp stores its 32 words (128 B) coalesced.
+// One chunk per warp and blocks in address order: the blocks in flight read
+// one contiguous region of the volume.  (Eight float4 loads per lane with a
+// four-way bit interleave after the ballots were 4-6 % slower for one
+// isovalue and issue bound for several.)
 //
 // The same step leaves a summary of its 32 words: sums[ch] = {mixed, ones},
 // bit w of `mixed` set when word 32*ch + w has nodes on both sides, bit w of
@@ -313,50 +309,6 @@ __device__ __forceinline__ void store_summary(uint2* sums, int64_t ch, uint32_t 
   const uint32_t mixed = __ballot_sync(0xffffffffu, word != 0u && word != 0xffffffffu);
   const uint32_t ones = __ballot_sync(0xffffffffu, word == 0xffffffffu);
   if (lane == 0) sums[ch] = make_uint2(mixed, ones);
-}
-
-__global__ void __launch_bounds__(kThreads)
-k_fe_threshold_v4(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
-                  uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
-                  uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks,
-                  int64_t ws_stride, const float* const* vols) {
-  // A batch of same-shape blocks: blockIdx.z picks the block.
-  if (vols) v = vols[blockIdx.z];
-  bits = shift_ptr(bits, (int64_t)blockIdx.z * ws_stride);
-  sums = shift_ptr(sums, (int64_t)blockIdx.z * ws_stride);
-  // nfull = chunks with all 1024 nodes present; a ragged last chunk (if
-  // any) is done by k_fe_threshold_scalar.
-  const int lane = threadIdx.x & 31;
-  const int64_t ch = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
-    const int t = threadIdx.x >> 3;
-    if (t < niso) bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;  // padding
-    if (t < niso && (threadIdx.x & 7) < 2)
-      sums[t * sums_stride + nchunks + (threadIdx.x & 7)] = make_uint2(0u, 0u);
-  }
-  if (ch >= nfull) return;  // whole warps only
-  const float4* __restrict__ v4 = reinterpret_cast<const float4*>(v) + (ch << 8);
-  float4 x[8];
-#pragma unroll
-  for (int q = 0; q < 8; ++q) x[q] = __ldcs(v4 + q * 32 + lane);
-  const int64_t wi = (ch << 5) + lane;
-  const int sh = (lane & 3) * 8;
-  for (int t = 0; t < niso; ++t) {
-    const float th = iso.v[t];
-    uint32_t word = 0;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const uint32_t b0 = __ballot_sync(0xffffffffu, x[q].x > th);
-      const uint32_t b1 = __ballot_sync(0xffffffffu, x[q].y > th);
-      const uint32_t b2 = __ballot_sync(0xffffffffu, x[q].z > th);
-      const uint32_t b3 = __ballot_sync(0xffffffffu, x[q].w > th);
-      if ((lane >> 2) == q)
-        word = spread8(b0 >> sh) | (spread8(b1 >> sh) << 1) |
-               (spread8(b2 >> sh) << 2) | (spread8(b3 >> sh) << 3);
-    }
-    bits[t * bits_stride + wi] = word;
-    store_summary(sums + t * sums_stride, ch, word, lane);
-  }
 }
 
 template <int NISO>
@@ -391,17 +343,18 @@ __device__ __forceinline__ void threshold_multi_body(const float* __restrict__ p
   }
 }
 
-// Several isovalues: lane l loads nodes l, 32 + l, ..., 992 + l of the chunk
-// (32 coalesced 128-byte loads per warp), so that each ballot is directly
-// the bit word of 32 consecutive nodes and no interleave is needed -- per
-// isovalue 32 compares, 32 ballots and 32 selects instead of the float4
-// layout's ballots plus four-way interleave, which leaves the kernel issue
-// bound once it runs for several isovalues.  The isovalue count is a
-// template parameter, so the isovalues' ballot chains of one node column
-// interleave (independent work for the scheduler) and share the lane test.
-// Full chunks only, like v4.
-__global__ void __launch_bounds__(kThreads, 5)
-k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, int niso,
+// The isovalue count is a template parameter, so that the isovalues' ballot
+// chains of one node column interleave (independent work for the scheduler)
+// and share the lane test.  Several isovalues are issue bound: they run in
+// 128-thread blocks at 12 per SM (48 warps), one isovalue in 256-thread
+// blocks at 5 per SM.  Full chunks only; block 0 also zeroes the padding
+// past the last word and the last summary.
+template <int NISO>
+constexpr int threshold_block() { return NISO == 1 ? 256 : 128; }
+
+template <int NISO>
+__global__ void __launch_bounds__(threshold_block<NISO>(), NISO == 1 ? 5 : 12)
+k_fe_threshold_words(const float* __restrict__ v, int64_t nfull, IsoParams iso,
                      uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
                      uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks,
                      int64_t ws_stride, const float* const* vols) {
@@ -411,25 +364,37 @@ k_fe_threshold_multi(const float* __restrict__ v, int64_t nfull, IsoParams iso, 
   sums = shift_ptr(sums, (int64_t)blockIdx.z * ws_stride);
   const int lane = threadIdx.x & 31;
   const int64_t ch = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (blockIdx.x == 0 && threadIdx.x < 8 * TKMC_MAX_ISO) {
+  if (blockIdx.x == 0 && threadIdx.x < 8 * NISO) {
     const int t = threadIdx.x >> 3;
-    if (t < niso) bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;  // padding
-    if (t < niso && (threadIdx.x & 7) < 2)
+    bits[t * bits_stride + nwords + (threadIdx.x & 7)] = 0u;  // padding
+    if ((threadIdx.x & 7) < 2)
       sums[t * sums_stride + nchunks + (threadIdx.x & 7)] = make_uint2(0u, 0u);
   }
   if (ch >= nfull) return;  // whole warps only
-  const float* __restrict__ p = v + (ch << 10) + lane;
-  switch (niso) {  // 1 <= niso <= TKMC_MAX_ISO, checked by the host
-    case 1: threshold_multi_body<1>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 2: threshold_multi_body<2>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 3: threshold_multi_body<3>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 4: threshold_multi_body<4>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 5: threshold_multi_body<5>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 6: threshold_multi_body<6>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 7: threshold_multi_body<7>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
-    case 8: threshold_multi_body<8>(p, iso, bits, bits_stride, sums, sums_stride, ch, lane); break;
+  threshold_multi_body<NISO>(v + (ch << 10) + lane, iso, bits, bits_stride, sums, sums_stride,
+                             ch, lane);
+}
+
+// Launch K1 over nfull full chunks (blocks.z = nb same-shape volumes).
+static void launch_threshold_words(int niso, int64_t nfull, unsigned nb, cudaStream_t st,
+                                   const float* v, const IsoParams& iso, uint32_t* bits,
+                                   int64_t bits_stride, int64_t nwords, uint2* sums,
+                                   int64_t sums_stride, int64_t nchunks, int64_t ws_stride,
+                                   const float* const* vols) {
+#define TKMC_K1(N)                                                                            \
+  case N: {                                                                                   \
+    const int64_t per = threshold_block<N>() / 32;                                            \
+    k_fe_threshold_words<N><<<dim3((unsigned)((nfull + per - 1) / per), 1, nb),                \
+                              threshold_block<N>(), 0, st>>>(v, nfull, iso, bits, bits_stride, \
+                                                             nwords, sums, sums_stride,        \
+                                                             nchunks, ws_stride, vols);        \
+    break;                                                                                    \
+  }
+  switch (niso) {  // 1 <= niso <= TKMC_MAX_ISO, checked by the callers
+    TKMC_K1(1) TKMC_K1(2) TKMC_K1(3) TKMC_K1(4) TKMC_K1(5) TKMC_K1(6) TKMC_K1(7) TKMC_K1(8)
     default: break;
   }
+#undef TKMC_K1
 }
 
 // Same result for a volume pointer that is not 16-byte aligned, and for the
@@ -3285,32 +3250,18 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   for (int t = 0; t < niso; ++t) iso.v[t] = isovalues[t];
   FeWsAll v = fe_views(f, ws, niso);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int vec = (reinterpret_cast<uintptr_t>(scalar) % 16) == 0;
   const int64_t nchunks = (f.V + 1023) / 1024;
-  // One 1024-node chunk per warp, blocks in address order: the blocks in
-  // flight at any moment read one contiguous region of the volume, which
-  // streams measurably faster from HBM than a persistent grid-stride loop
-  // (6.9 vs 6.0 TB/s on a 4 GiB volume).
   constexpr int kWarps = kThreads / 32;
   uint32_t* bits0 = v.iso[0].bits;
   uint2* sums0 = v.iso[0].sums;
-  // Full chunks: float4 loads for one isovalue (16-byte-aligned volumes),
-  // one-word ballots for several (any alignment).
-  const int64_t nfull = (vec || niso > 1) ? f.V / 1024 : 0;
+  const int64_t nfull = f.V / 1024;  // full chunks (any 4-byte alignment)
   if (nfull > 0) {
-    const int64_t gb = (nfull + kWarps - 1) / kWarps;
-    if (gb > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
-    if (niso == 1)
-      k_fe_threshold_v4<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
-                                                           f.bits_stride, f.nwords, sums0,
-                                                           f.sums_stride, nchunks, 0, nullptr);
-    else
-      k_fe_threshold_multi<<<(unsigned)gb, kThreads, 0, st>>>(scalar, nfull, iso, niso, bits0,
-                                                              f.bits_stride, f.nwords, sums0,
-                                                              f.sums_stride, nchunks, 0, nullptr);
+    if (nfull / 4 > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
+    launch_threshold_words(niso, nfull, 1, st, scalar, iso, bits0, f.bits_stride, f.nwords,
+                           sums0, f.sums_stride, nchunks, 0, nullptr);
     TK_LAUNCHED();
   }
-  if (nfull < nchunks) {  // unaligned volume, or the ragged last chunk
+  if (nfull < nchunks) {  // the ragged last chunk
     const int64_t rest = nchunks - nfull;
     const int64_t gb = (rest + kWarps - 1) / kWarps;
     if (gb > 0x7fffffffLL) return set_err(TKMC_ERR_INVALID_ARG, "volume too large");
@@ -3586,14 +3537,11 @@ int tkmc_fe_count_batch(const float* const* vols, int64_t nblocks, int64_t nx, i
   IsoParams iso{};
   for (int t = 0; t < niso; ++t) iso.v[t] = isovalues[t];
   const int64_t nchunks = (f.V + 1023) / 1024, nfull = f.V / 1024;
-  constexpr int kWarps = kThreads / 32;
   const unsigned nb = (unsigned)nblocks;
-  // Device pointers of unknown alignment: the scalar-load layout for full
-  // chunks, the scalar kernel for a ragged last chunk.
+  // Full chunks by the word kernel, a ragged last chunk by the scalar one.
   if (nfull > 0) {
-    k_fe_threshold_multi<<<dim3((unsigned)((nfull + kWarps - 1) / kWarps), 1, nb), kThreads, 0, st>>>(
-        nullptr, nfull, iso, niso, v.iso[0].bits, f.bits_stride, f.nwords, v.iso[0].sums,
-        f.sums_stride, nchunks, v.stride, vols);
+    launch_threshold_words(niso, nfull, nb, st, nullptr, iso, v.iso[0].bits, f.bits_stride,
+                           f.nwords, v.iso[0].sums, f.sums_stride, nchunks, v.stride, vols);
     TK_LAUNCHED();
   }
   if (nfull < nchunks) {
