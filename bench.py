@@ -497,7 +497,7 @@ def main():
                        "input smaller than 2x L2: numbers include L2 reuse between steps"),
             },
             "roofline": {
-                "bound": "hbm", "kernel": "k_fe_threshold (K1: volume -> node bitmask)",
+                "bound": "hbm", "kernel": "k_fe_threshold_words (K1: volume -> node bitmask)",
                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": traffic, "peak_source": peak_src,
                 "algorithmic_bytes_per_launch": alg_k1,
