@@ -2152,10 +2152,15 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
                   shZ = base_out(A, bq, 2) - idZ;
   const long long outT = base_tri(A, bq);
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t grp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5; grp * 32 < n_own;
+  // Units per warp task: 32, or 16 when the units make at most one task of
+  // 32 per warp -- then the longest task, not the number of tasks, sets the
+  // kernel's time, and halving the units per task shortens it (the small
+  // slabs of 8 GPUs).
+  const int G = n_own > 32 * nwarps ? 32 : 16;
+  for (int64_t grp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5; grp * G < n_own;
        grp += nwarps) {
     // ---- lane = unit ----
-    const int64_t u = grp * 32 + lane;
+    const int64_t u = lane < G ? grp * G + lane : n_own;
     unsigned np = 0, nc = 0;
     uint32_t* rec = U + lane * kUS;
     if (u < n_own) {
