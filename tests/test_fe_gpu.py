@@ -337,3 +337,31 @@ def test_block_batches_match_oracle(tack, oracle, cells, nblocks):
         p0 += ref["points"].shape[0]
     np.testing.assert_array_equal(r["conn"], np.concatenate(conns))
     assert_points_identical(r["points"], np.concatenate(pts))
+
+
+def test_amr_blanking_style_masks_match_oracle(tack, oracle):
+    """Masks as amr_blanking.build_masks (amr_blanking.py:26) writes them:
+    per-cell flags DUPLICATECELL = 1 (ghost layers), REFINEDCELL = 8 (covered
+    by a finer level) and both (9).  Any nonzero flag removes the cell's
+    triangles (flying_edges.py:441-477); points stay.  Word-aligned and
+    ragged row lengths, one block through flying_edges_multiblock."""
+    from tack_b200 import workloads
+    for shape in ((64, 48, 40), (70, 33, 29)):
+        nx, ny, nz = shape[0] - 1, shape[1] - 1, shape[2] - 1
+        v = workloads.generate("gyroid", shape).cpu().numpy()
+        mask = np.zeros((nz, ny, nx), np.int32)
+        mask[:2] |= 1                 # ghost layers at both z ends and one y side
+        mask[-2:] |= 1
+        mask[:, :2] |= 1
+        mask[10:20, 8:24, 5:40] |= 8  # a refined box, overlapping a ghost layer
+        mask = mask.reshape(-1)
+        g = (nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+        blk = {"scalar": _upload(tack, v, tack.f32), "grid": tack.UniformGrid(*g),
+               "mask": _upload(tack, mask, tack.i32)}
+        got = tack.flying_edges_multiblock([blk], 0.0)
+        ref = oracle.flying_edges(v, oracle.Grid(*g), 0.0, mask)
+        np.testing.assert_array_equal(got["conn"], ref["conn"])
+        assert_points_identical(got["points"], ref["points"])
+        plain = oracle.flying_edges(v, oracle.Grid(*g), 0.0)
+        assert ref["total_tris"] < plain["total_tris"]
+        assert ref["total_points"] == plain["total_points"]
