@@ -6,13 +6,17 @@
 Workload (default): 1024^3 f32 volume, sum of 32 seeded Gaussian blobs,
 isovalue 0.5 -- the configuration the metric is quoted on at 1/2/4/8 GPUs.
 The volume is z-slab sharded across N GPUs (one process per GPU, launched by
-torchrun for N > 1): each rank classifies/counts/scans its slab, one NCCL
-all-gather exchanges the per-rank totals, each rank emits its slices of the
-single-volume output.  Total work is fixed as N grows (strong scaling).
+torchrun for N > 1): each rank classifies/counts/scans its slab, the
+per-rank totals are exchanged on the device (by default one kernel storing
+them into every rank's memory over NVLink, `--exchange nccl` for an NCCL
+all-gather), each rank emits its slices of the single-volume output.  Total
+work is fixed as N grows (strong scaling).  At N > 1 every rank's slices are
+then compared, byte for byte, with the same rows of a single-GPU run of the
+whole volume on rank 0 (`parity` in the JSON line).
 
 A step = one isosurface of the whole volume from resident f32 values to
 resident points + connectivity: classify, count + scan, the per-rank totals
-all-gathered on the device, device-side planning of the output bases, emit,
+exchanged on the device, device-side planning of the output bases, emit,
 and an asynchronous copy of the totals to pinned host memory.  Output buffers
 are allocated once, at this volume's exact size, from one host-planned run
 before the timed steps (as when a caller processes a sequence of volumes);
@@ -21,11 +25,14 @@ the whole volume per second over K timed steps (CUDA events, max over ranks).  `
 through the public API from pinned host memory: each step copies the volume
 host->device, runs flying_edges, copies points and connectivity back.
 
-The reference arm (--impl reference) times the CPU parity oracle -- a C
-restatement of the reference's flying-edges kernels with its host
-orchestration, using every host core -- on a bounded z-slab of the same
-volume (the reference itself is a Python package whose JIT path cannot be
-shipped to the GPU host).
+The reference arm (--impl reference) times the reference's own flying_edges
+on its CPU backend (tack.cpu, llvmlite JIT, one thread per physical core),
+imported from a copy of its Python sources in baseline/_ref
+(`bench.py --install-reference <checkout>` makes the copy), on a bounded
+sample of the same volume: a few z-slabs spread evenly over its depth.  The
+C restatement of the same algorithm (the parity oracle) is timed beside it
+on the same sample.  The GPU arm's cpu_baseline runs the same two legs on
+the same sample.
 """
 
 import argparse
@@ -61,7 +68,11 @@ def parse_args():
     ap.add_argument("--size", type=int, nargs=3, default=None,
                     help="override the volume's node counts (nx ny nz)")
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-steps", type=int, default=5,
+                    help="timed steps of each CPU leg of cpu_baseline (after 2 untimed)")
+    ap.add_argument("--install-reference", metavar="CHECKOUT", default=None,
+                    help="copy the reference's Python sources from a berkgeveci/tack "
+                         "checkout into baseline/_ref and exit")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
@@ -209,34 +220,192 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- reference arm
+#
+# The CPU legs time the reference's own flying edges (tack.cpu, its llvmlite
+# JIT backend) and, beside it, the C port of the same algorithm (the parity
+# oracle), on the same bounded sample of the workload: a few z-slabs spread
+# evenly over the volume (so the surface's density along z is represented),
+# every slab an independent flying_edges call on its own node planes.  The
+# reference arm (--impl reference) and the GPU arm's cpu_baseline use the
+# same sample and the same method, so they measure the same thing.
 
-def cpu_sample_rate(volume_host_planes, shape, k0, isos, nthreads, min_seconds, max_calls=50):
-    """Oracle flying_edges on a z-slab; returns (Gcells/s, per-call seconds, cells)."""
-    from oracle import oracle
-    nx, ny, _ = shape
-    nz_cells = volume_host_planes.size // (nx * ny) - 1
-    g = oracle.Grid(nx - 1, ny - 1, nz_cells, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0)
-    cells = (nx - 1) * (ny - 1) * nz_cells
-    times = []
-    t_start = time.perf_counter()
-    while True:
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+REF_TREES = (("tack-core", "src"), ("tack-vis", "src"))
+CPU_SAMPLE_CELLS = 1.4e8   # cells per step of the CPU sample, all isovalues together
+CPU_SAMPLE_SLABS = 8
+
+
+def install_reference(checkout):
+    """Copy the reference's pure-Python source trees (packages/tack-core/src,
+    packages/tack-vis/src of a berkgeveci/tack checkout) into baseline/_ref,
+    where the reference arm imports them from.  The reference's own build
+    backend is not installable offline; the sources need no build."""
+    import shutil
+    for pkg, sub in REF_TREES:
+        src = os.path.join(checkout, "packages", pkg, sub)
+        dst = os.path.join(REF_DIR, pkg, sub)
+        if not os.path.isdir(src):
+            raise FileNotFoundError(src)
+        if os.path.isdir(dst):
+            shutil.rmtree(dst)
+        shutil.copytree(src, dst, ignore=shutil.ignore_patterns("__pycache__", "*.pyc"))
+    return REF_DIR
+
+
+def load_reference_cpu():
+    """The reference's tack on its CPU backend, imported from baseline/_ref.
+    Returns (flying_edges, UniformGrid, field factory, f32 dtype, threads)."""
+    paths = [os.path.join(REF_DIR, pkg, sub) for pkg, sub in REF_TREES]
+    missing = [p for p in paths if not os.path.isdir(os.path.join(p, "tack"))]
+    if missing:
+        raise ImportError(f"no copy of the reference under {missing[0]} "
+                          "(bench.install_reference copies it from a checkout)")
+    for p in reversed(paths):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import tack as ref_tack
+    from tack.runtime.dispatch import get_backend
+    ref_tack.init(ref_tack.cpu)
+    from tack.algorithms.flying_edges import UniformGrid, flying_edges
+    return flying_edges, UniformGrid, ref_tack.field, ref_tack.f32, get_backend().num_threads
+
+
+def cpu_sample_bounds(shape, niso):
+    """Node-plane ranges [k0, k1) of the CPU sample: the whole volume when it
+    is small, else CPU_SAMPLE_SLABS slabs centred at evenly spaced depths,
+    their thickness set so a step is about CPU_SAMPLE_CELLS cells (all
+    isovalues together), at least two cell layers each."""
+    nx, ny, nz = shape
+    per_plane = (nx - 1) * (ny - 1) * niso
+    if per_plane * (nz - 1) <= CPU_SAMPLE_CELLS:
+        return [(0, nz)]
+    layers = int(max(2, round(CPU_SAMPLE_CELLS / (CPU_SAMPLE_SLABS * per_plane))))
+    planes = min(nz, layers + 1)
+    out = []
+    for i in range(CPU_SAMPLE_SLABS):
+        c = (2 * i + 1) * nz // (2 * CPU_SAMPLE_SLABS)
+        k0 = min(max(0, c - planes // 2), nz - planes)
+        out.append((k0, k0 + planes))
+    return out
+
+
+class CpuSample:
+    """The slabs of the CPU sample as host f32 arrays (generated on the GPU
+    when there is one)."""
+
+    def __init__(self, config, shape, isos, device, volume=None):
+        from tack_b200 import workloads
+        self.shape, self.isos = shape, list(isos)
+        self.bounds = cpu_sample_bounds(shape, len(self.isos))
+        nx, ny, nz = shape
+        self.slabs = []
+        for k0, k1 in self.bounds:
+            if volume is not None:  # the resident volume, planes [k0, k1)
+                v = volume.view(nz, ny, nx)[k0:k1].reshape(-1).cpu().numpy()
+            else:
+                v = workloads.generate(config, shape, k0, k1, device=device).cpu().numpy()
+            self.slabs.append((k0, k1, v))
+        self.cells = sum((nx - 1) * (ny - 1) * (k1 - k0 - 1) for k0, k1 in self.bounds)
+
+    def describe(self):
+        nx, ny, nz = self.shape
+        if self.bounds == [(0, nz)]:
+            where = "the whole volume"
+        else:
+            where = ", ".join(f"[{a},{b})" for a, b in self.bounds)
+            where = f"node planes {where}"
+        return (f"{where} of the {nx}x{ny}x{nz} volume: {self.cells} cells per isovalue, "
+                f"one flying_edges call per slab and isovalue per step")
+
+
+def time_reference_cpu(sample, steps, warmup):
+    """Per-step seconds of the reference's tack.cpu flying_edges over the
+    sample (fields created once, outside the timing, as resident inputs)."""
+    fe, Grid, field, f32, threads = load_reference_cpu()
+    nx, ny, _ = sample.shape
+    calls = []
+    for k0, k1, v in sample.slabs:
+        f = field(dtype=f32, shape=(v.size,))
+        f.from_numpy(v)
+        calls.append((f, Grid(nx - 1, ny - 1, k1 - k0 - 1, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0)))
+
+    def step():
         t0 = time.perf_counter()
-        oracle.flying_edges_isovalues(volume_host_planes, g, isos, nthreads=nthreads)
-        times.append(time.perf_counter() - t0)
-        if (time.perf_counter() - t_start >= min_seconds and len(times) >= 3) or \
-                len(times) >= max_calls:
-            break
-    t = statistics.median(times)
-    return cells / t / 1e9, t, cells
+        for f, g in calls:
+            for iso in sample.isos:
+                fe(f, g, iso)
+        return time.perf_counter() - t0
+
+    for _ in range(warmup):
+        step()
+    return [step() for _ in range(steps)], threads
 
 
-def host_slab(args, shape, planes, device):
-    """The middle `planes` node planes of the workload, as a host array."""
-    from tack_b200 import workloads
-    nz = shape[2]
-    k0 = max(0, nz // 2 - planes // 2)
-    v = workloads.generate(args.config, shape, k0, k0 + planes, device=device)
-    return v.cpu().numpy(), k0
+def time_port_cpu(sample, steps, warmup):
+    """Per-step seconds of the C port (the parity oracle, pthreads over rows,
+    every host thread) over the sample."""
+    from oracle import oracle
+    oracle.build()
+    nthreads = oracle.num_threads(0)
+    nx, ny, _ = sample.shape
+    calls = [(v, oracle.Grid(nx - 1, ny - 1, k1 - k0 - 1, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0))
+             for k0, k1, v in sample.slabs]
+
+    def step():
+        t0 = time.perf_counter()
+        for v, g in calls:
+            oracle.flying_edges_isovalues(v, g, sample.isos, nthreads=nthreads)
+        return time.perf_counter() - t0
+
+    for _ in range(warmup):
+        step()
+    return [step() for _ in range(steps)], nthreads
+
+
+def host_cores():
+    """Physical cores and the CPU model of this host (from lscpu)."""
+    info = {"logical": os.cpu_count()}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        kv = dict(line.split(":", 1) for line in out.splitlines() if ":" in line)
+        kv = {k.strip(): v.strip() for k, v in kv.items()}
+        info["model"] = kv.get("Model name")
+        sockets = int(kv.get("Socket(s)", "1") or 1)
+        cores = int(kv.get("Core(s) per socket", "0") or 0)
+        if cores:
+            info["physical"] = sockets * cores
+    except (OSError, ValueError, subprocess.SubprocessError):
+        pass
+    return info
+
+
+def cpu_legs(sample, steps, warmup, port_steps=3):
+    """Both CPU legs on the sample: the reference's tack.cpu (kind
+    "reference"; the port alone, kind "port", when the reference cannot be
+    imported here) and the C port beside it.  Returns the cpu_baseline dict."""
+    cores = host_cores()
+    legs = {}
+    try:
+        t, threads = time_reference_cpu(sample, steps, warmup)
+        legs["reference"] = {"value": sample.cells * len(sample.isos) * len(t) / sum(t) / 1e9,
+                             "cores": threads, "kind": "reference",
+                             "seconds_per_step": statistics.median(t), "steps": len(t),
+                             "what": "the reference's flying_edges on tack.cpu (llvmlite JIT), "
+                                     "imported from its source tree in baseline/_ref, "
+                                     "TACK_CPU_THREADS unset (one thread per physical core)"}
+    except Exception as e:  # the reference could not be imported or run here
+        legs["reference_error"] = f"{type(e).__name__}: {e}"
+    t, nthreads = time_port_cpu(sample, port_steps, 1)
+    legs["port"] = {"value": sample.cells * len(sample.isos) * len(t) / sum(t) / 1e9,
+                    "cores": nthreads, "kind": "port", "seconds_per_step": statistics.median(t),
+                    "steps": len(t),
+                    "what": "the C restatement of the reference's kernels and host "
+                            "orchestration (the parity oracle), pthreads over rows"}
+    head = legs.get("reference") or legs["port"]
+    out = {"value": head["value"], "unit": "Gcells/s", "cores": head["cores"],
+           "kind": head["kind"], "sample": sample.describe(), "host_cores": cores}
+    out.update(legs)
+    return out
 
 
 def run_reference(args):
@@ -244,47 +413,30 @@ def run_reference(args):
     if rank != 0:
         return 0
     import torch
-    from oracle import oracle
     from tack_b200 import workloads
-    oracle.build()
     cfg = workloads.CONFIGS[args.config]
     shape = tuple(args.size) if args.size else cfg["shape"]
     device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
-    nthreads = oracle.num_threads(0)
-    # Size the slab so that warmup + steps fit in about two minutes.
-    calib, k0 = host_slab(args, shape, 8, device)
-    rate, _, _ = cpu_sample_rate(calib, shape, k0, cfg["isovalues"], nthreads, 0.0, max_calls=2)
-    budget = 120.0 / max(1, args.steps + args.warmup)
-    cells_per_plane = (shape[0] - 1) * (shape[1] - 1)
-    planes = int(np.clip(budget * rate * 1e9 / cells_per_plane, 2, min(128, shape[2])))
-    vol, k0 = host_slab(args, shape, planes, device)
-    nz_cells = planes - 1
-    g = oracle.Grid(shape[0] - 1, shape[1] - 1, nz_cells, 0.0, 0.0, float(k0), 1.0, 1.0, 1.0)
-    cells = cells_per_plane * nz_cells
-    for _ in range(args.warmup):
-        oracle.flying_edges_isovalues(vol, g, cfg["isovalues"], nthreads=nthreads)
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        oracle.flying_edges_isovalues(vol, g, cfg["isovalues"], nthreads=nthreads)
-        times.append(time.perf_counter() - t0)
-    total = sum(times)
-    value = cells * args.steps / total / 1e9
-    sample = (f"node planes [{k0},{k0 + planes}) of the {shape[0]}x{shape[1]}x{shape[2]} "
-              f"{args.config} volume ({cells} cells) per step")
+    sample = CpuSample(args.config, shape, cfg["isovalues"], device)
+    # JIT compilation takes the first calls: at least two untimed steps.
+    base = cpu_legs(sample, args.steps, max(2, args.warmup))
+    head = base.get("reference") or base["port"]
+    value = head["value"]
+    ms = head["seconds_per_step"] * 1e3
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcells/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": total / args.steps * 1e3, "higher_is_better": True,
+        "n_gpus": world, "steps": args.steps, "warmup": max(2, args.warmup),
+        "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_name(args.config, shape, cfg["isovalues"]),
-                   "volume_nodes": list(shape), "isovalues": cfg["isovalues"]},
-        "cpu_baseline": {"value": value, "unit": "Gcells/s", "cores": nthreads, "kind": "port",
-                         "sample": sample},
+                   "volume_nodes": list(shape), "isovalues": cfg["isovalues"],
+                   "sample": sample.describe()},
+        "cpu_baseline": base,
         "e2e": {"value": value, "unit": "Gcells/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-        "note": ("CPU parity oracle (C restatement of the reference's flying-edges kernels "
-                 "and host orchestration, pthreads over rows), all host threads"),
+        "note": ("host cores only; value = cells of the sample x isovalues per second of "
+                 "the reference's own flying_edges on tack.cpu (kind 'reference'), or of "
+                 "the C port when the reference cannot be imported (kind 'port')"),
     }
     print(json.dumps(out), flush=True)
     return 0
@@ -302,6 +454,9 @@ def workload_name(config, shape, isos):
 
 def main():
     args = parse_args()
+    if args.install_reference:
+        print(install_reference(args.install_reference))
+        return 0
     if args.impl == "reference":
         return run_reference(args)
     import torch
@@ -432,12 +587,39 @@ def main():
         dist.all_gather(allk1, k1_rank)
         k1_rank = min(allk1, key=lambda t: float(t[0]))
     k1_nodes, k1_ms = float(k1_rank[1]), float(k1_rank[2])
-    stats = torch.tensor([ms, k1, k2, k3, host], dtype=torch.float64, device=dev)
+    # Every rank's phase times, so the slowest rank and the time the others
+    # spend waiting for it in the exchange are visible.
+    mine = torch.tensor([ms, k1, k2, host, k3, float(own_p), float(own_t)], dtype=torch.float64,
+                        device=dev)
+    per_rank = [mine]
     if world > 1:
-        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
-    ms, k1, k2, k3, host = (float(x) for x in stats.cpu())
+        per_rank = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(per_rank, mine)
+    per_rank = np.stack([t.cpu().numpy() for t in per_rank])
+    ms, k1, k2, host, k3 = (float(x) for x in per_rank[:, :5].max(axis=0))
     total_points = int(bases["totals"][:, 0].sum())
     total_tris = int(bases["totals"][:, 1].sum())
+    ranks = None
+    if world > 1:
+        arrive = per_rank[:, 1] + per_rank[:, 2]  # threshold + count: ready to exchange
+        ranks = {
+            "k1_threshold_ms": [round(float(x), 4) for x in per_rank[:, 1]],
+            "k2_count_scan_ms": [round(float(x), 4) for x in per_rank[:, 2]],
+            "exchange_plan_ms": [round(float(x), 4) for x in per_rank[:, 3]],
+            "k3_emit_ms": [round(float(x), 4) for x in per_rank[:, 4]],
+            "points": [int(x) for x in per_rank[:, 5]],
+            "triangles": [int(x) for x in per_rank[:, 6]],
+            "slowest_to_exchange": int(np.argmax(arrive)),
+            "arrival_skew_ms": round(float(arrive.max() - arrive.min()), 4),
+            "exchange_wait_spread_ms": round(float(per_rank[:, 3].max() - per_rank[:, 3].min()), 4),
+            "note": ("phase means over ordinary (not graph) steps on each rank; a rank's "
+                     "exchange_plan time is mostly its wait for the last rank to arrive, so "
+                     "the spread of those times is the arrival skew seen on the device"),
+        }
+
+    # ---- parity of the timed path's output (outside the timed region) -----
+    parity = check_parity(args, tack, torch, dist, shape, isos, grid, first["all_counts"],
+                          pts_buf, conn_buf, world, rank, dev)
 
     # ---- next filter on the same surface: vertex normals (one GPU) --------
     normals = soup = None
@@ -452,21 +634,12 @@ def main():
         e2e = run_e2e(args, tack, torch, dist, vol, grid, plan, eng, isos, world, rank, dev,
                       cells)
 
-    # ---- CPU baseline (oracle, host cores), N == 1 only ------------------------
+    # ---- CPU baseline (host cores), N == 1 only: the same sample and method
+    # as the reference arm (bench.py --impl reference) ----------------------
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
-        from oracle import oracle
-        oracle.build()
-        nthreads = oracle.num_threads(0)
-        planes = min(64, nzn)
-        k0 = max(0, nzn // 2 - planes // 2)
-        slab = vol.view(nzn, nyn, nxn)[k0:k0 + planes].reshape(-1).cpu().numpy()
-        rate, t_call, scells = cpu_sample_rate(slab, shape, k0, isos, nthreads, args.cpu_seconds)
-        cpu = {"value": rate, "unit": "Gcells/s", "cores": nthreads, "kind": "port",
-               "sample": (f"node planes [{k0},{k0 + planes}) of the same volume "
-                          f"({scells} cells), median of repeated calls over "
-                          f">= {args.cpu_seconds:.0f} s"),
-               "seconds_per_call": t_call}
+        sample = CpuSample(args.config, shape, isos, dev, volume=vol)
+        cpu = cpu_legs(sample, args.cpu_steps, 2)
 
     if world > 1:
         dist.barrier()
@@ -509,7 +682,10 @@ def main():
                 "frac_of_aggregate_peak": step_bytes / (ms / K * 1e-3) / 1e9 / (peak * world),
             },
             "kernels_ms": {"k1_threshold": k1, "k2_count_scan": k2,
-                           "totals_gather_plan": host, "k3_emit": k3},
+                           "totals_gather_plan": host, "k3_emit": k3,
+                           "note": "each phase's max over ranks"},
+            "per_rank": ranks,
+            "parity": parity,
             "outputs": {"points": total_points, "triangles": total_tris},
             "compute_normals": normals,
             "marching_cubes_soup": soup,
@@ -525,6 +701,80 @@ def main():
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def check_parity(args, tack, torch, dist, shape, isos, grid, all_counts, pts_buf, conn_buf,
+                 world, rank, dev):
+    """Every rank's output slices from the timed path (the last graph replay)
+    against the same rows of one single-GPU flying_edges call on the whole
+    volume, run on rank 0: points compared as bit patterns, conn exactly.
+    Ranks send their slices to rank 0 (NCCL point-to-point); every rank
+    raises if any slice differs.  Outside the timed region."""
+    from tack_b200 import workloads
+    from tack_b200.distributed import slab_bases
+    allc = np.asarray(all_counts, np.int64)  # [world, niso, 4]
+    niso = allc.shape[1]
+    sizes = [(int(allc[r, :, :3].sum()), int(allc[r, :, 3].sum())) for r in range(world)]
+    ok = torch.ones(1, dtype=torch.int32, device=dev)
+    checked_pts = checked_tris = 0
+    info = {}
+    if rank == 0:
+        nx, ny, nz = shape
+        whole = workloads.generate(args.config, shape, 0, nz, device=dev)
+        ref = tack.flying_edges(whole, grid, isos if len(isos) > 1 else isos[0],
+                                copy_to_host=False)
+        del whole
+        ref_p = ref["points_field"].tensor.view(torch.int32).view(-1, 3)
+        ref_c = ref["conn_field"].tensor.view(-1, 3)
+        P_all, T_all = ref["total_points"], ref["total_tris"]
+        good = (P_all == int(allc[:, :, :3].sum())) and (T_all == int(allc[:, :, 3].sum()))
+        for r in range(world):
+            P, T = sizes[r]
+            if r == 0:
+                p = pts_buf[:P * 3]
+                c = conn_buf[:T * 3]
+            else:
+                p = torch.empty(P * 3, dtype=torch.float32, device=dev)
+                c = torch.empty(T * 3, dtype=torch.int32, device=dev)
+                if P:
+                    dist.recv(p, src=r)
+                if T:
+                    dist.recv(c, src=r)
+            p = p.view(torch.int32).view(-1, 3)
+            c = c.view(-1, 3)
+            b = slab_bases(allc, r)
+            for q in range(niso):
+                for sct in range(3):
+                    n = int(allc[r, q, sct])
+                    lo, go = int(b["out_base"][q, sct]), int(b["pt_global_out"][q, sct])
+                    good &= bool(torch.equal(p[lo:lo + n], ref_p[go:go + n]))
+                    checked_pts += n
+                n = int(allc[r, q, 3])
+                lo, go = int(b["tri_out"][q]), int(b["tri_global"][q])
+                good &= bool(torch.equal(c[lo:lo + n], ref_c[go:go + n]))
+                checked_tris += n
+        good &= checked_pts == P_all and checked_tris == T_all
+        ok.fill_(1 if good else 0)
+        info = {"points": P_all, "triangles": T_all, "points_checked": checked_pts,
+                "triangles_checked": checked_tris}
+        del ref, ref_p, ref_c
+    else:
+        P, T = sizes[rank]
+        if P:
+            dist.send(pts_buf[:P * 3].contiguous(), dst=0)
+        if T:
+            dist.send(conn_buf[:T * 3].contiguous(), dst=0)
+    if world > 1:
+        dist.broadcast(ok, src=0)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    if int(ok.item()) != 1:
+        raise RuntimeError("parity: the timed path's output differs from the single-GPU "
+                           "flying_edges of the whole volume")
+    info.update({"checked": True, "ranks_equal": world,
+                 "against": "one single-GPU tack_b200.flying_edges call on the whole volume "
+                            "(rank 0); points bit for bit, conn exact, every row once"})
+    return info
 
 
 def time_normals(tack, torch, points, conn, n_pts, n_tris, stream, reps=20):

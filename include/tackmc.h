@@ -4,9 +4,12 @@
  *
  * Every entry point takes plain pointers, 64-bit sizes and a CUDA stream
  * passed as `void*` (NULL = legacy default stream).  Device pointers must
- * belong to the device that is current on the calling thread.  No entry
- * point allocates or frees device memory: scratch space is a caller-provided
- * workspace whose size the matching *_workspace_bytes() function returns.
+ * belong to the device that is current on the calling thread.  Scratch
+ * space is a caller-provided workspace whose size the matching
+ * *_workspace_bytes() function returns.  The only entry points that allocate
+ * or free device memory are tkmc_exchange_create (one small buffer per rank,
+ * shared with the other ranks through CUDA IPC) and tkmc_exchange_destroy,
+ * which frees it.
  * Every entry point returns an int status (TKMC_OK == 0); on failure
  * tkmc_last_error() returns a thread-local message.  Nothing exits, traps or
  * waits without a bound.
@@ -82,7 +85,11 @@ size_t tkmc_scan_workspace_bytes(int64_t n);
  * out[i] = sum(in[0..i]).  Sums are carried in int64 and stored as int32
  * (two's-complement wrap, as the reference's int32 fields do); *total (HOST,
  * may be NULL) receives the exact int64 sum of all n values.  `in` and `out`
- * may alias.  Synchronises `stream` when total != NULL.
+ * may alias.  Synchronises `stream` once, to read the total and the look-back
+ * error word back, also when total is NULL: an expired look-back wait returns
+ * TKMC_ERR_DEVICE_TIMEOUT either way.  While `stream` is being captured into
+ * a CUDA graph nothing is read back (total must then be NULL) and no timeout
+ * can be reported.
  * Replaces: scan.py:81-102 (exclusive_scan) and scan.py:105-123
  * (inclusive_scan). */
 int tkmc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive,
@@ -273,6 +280,10 @@ int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx,
  *           (tkmc_exchange_handle_bytes bytes) for the other ranks.
  *   connect: open every rank's handle (handles in rank order).
  *   plan: after tkmc_fe_scan on this rank's slab; bases_dev as tkmc_fe_plan.
+ *         Each slot of the gathered totals carries its epoch; a slot from
+ *         another epoch (a peer out of step after an expired wait) records
+ *         TKMC_ERR_DEVICE_TIMEOUT as well.  After that error, destroy the
+ *         exchange on every rank and create it again.
  *   destroy: after every rank has finished its last plan (a barrier).
  */
 size_t tkmc_exchange_handle_bytes(void);
@@ -306,7 +317,10 @@ int tkmc_fe_copy_status(int64_t nx, int64_t ny, int64_t nz, int niso,
  * (shared_output = 0: the part's x, y, z points then its triangles, per
  * isovalue; the sums of tack_b200.distributed.slab_bases) or in one shared
  * single-volume output (shared_output != 0: rows = ids, triangle rows
- * global).  Asynchronous. */
+ * global).  When the global point total (all ranks and isovalues) exceeds
+ * INT32_MAX, the id bases are set negative: the emit kernels then write
+ * nothing and record TKMC_ERR_OVERFLOW, which tkmc_fe_check returns.
+ * Asynchronous. */
 int tkmc_fe_plan(const int64_t* all_counts_dev, int world, int rank, int niso,
                  int shared_output, int64_t* bases_dev, void* stream);
 
@@ -319,7 +333,8 @@ int tkmc_fe_clear_capacity_error(int64_t nx, int64_t ny, int64_t nz, int niso,
 
 /* Synchronise `stream` and report any error the device recorded in the
  * workspace during the last count/emit (TKMC_ERR_DEVICE_TIMEOUT,
- * TKMC_ERR_CAPACITY), else TKMC_OK. */
+ * TKMC_ERR_CAPACITY, TKMC_ERR_OVERFLOW from device-planned bases), else
+ * TKMC_OK. */
 int tkmc_fe_check(int64_t nx, int64_t ny, int64_t nz, int niso,
                   void* workspace, size_t workspace_bytes, void* stream);
 

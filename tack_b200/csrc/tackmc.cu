@@ -1419,6 +1419,17 @@ __device__ __forceinline__ void record_overflow(long long* info) {
   atomicExch((unsigned long long*)(info + 10), (unsigned long long)TKMC_ERR_CAPACITY);
 }
 
+// Device-planned bases whose global point total does not fit int32 ids are
+// negative (k_fe_plan_body).  The emit then writes nothing: thread 0 of each
+// block records TKMC_ERR_OVERFLOW (unless an earlier error is recorded) and
+// the whole block returns.  Host-given bases are never negative.
+__device__ __forceinline__ bool ids_overflow(long long id_base, long long* info) {
+  if (id_base >= 0) return false;
+  if (threadIdx.x == 0)
+    atomicCAS((unsigned long long*)(info + 10), 0ull, (unsigned long long)TKMC_ERR_OVERFLOW);
+  return true;
+}
+
 // Segmented (width S) inclusive scan.
 __device__ __forceinline__ unsigned seg_scan(unsigned x, int sl, int S) {
   for (int o = 1; o < S; o <<= 1) {
@@ -1494,6 +1505,7 @@ k_fe_emit_rows(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const long long shiftY = base_out(A, bq, 1) - idB[1];
   const long long shiftZ = base_out(A, bq, 2) - idB[2];
   const long long outT = base_tri(A, bq);
+  if (ids_overflow(idB[0], W.info)) return;
 
   for (int64_t grp = gw; grp * G < n_active; grp += nw) {
     // ---------------- phase 1: lane = (row segment, word) ----------------
@@ -1821,6 +1833,7 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const long long shiftY = base_out(A, bq, 1) - idY;
   const long long shiftZ = base_out(A, bq, 2) - idZ;
   const long long outT = base_tri(A, bq);
+  if (ids_overflow(idX, W.info)) return;
 
   for (int64_t grp = gw; grp * 32 < n_active; grp += nw) {
     // ---- rows: lane = one active row ----
@@ -2151,6 +2164,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const long long shX = base_out(A, bq, 0) - idX, shY = base_out(A, bq, 1) - idY,
                   shZ = base_out(A, bq, 2) - idZ;
   const long long outT = base_tri(A, bq);
+  if (ids_overflow(idX, W.info)) return;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   // Units per warp task: 32, or 16 when the units make at most one task of
   // 32 per warp -- then the longest task, not the number of tasks, sets the
@@ -2489,6 +2503,12 @@ __device__ void k_fe_plan_body(const long long* c, int world, int rank, int niso
     lp += own[0] + own[1] + own[2];
     lt += own[3];
   }
+  // Point ids are int32 in conn: a global point total above INT32_MAX
+  // cannot be emitted.  Negative id bases tell every emit kernel to write
+  // nothing and record TKMC_ERR_OVERFLOW (read back by tkmc_fe_check).
+  if (Pq > 0x7fffffffLL)
+    for (int q = 0; q < niso; ++q)
+      for (int s = 0; s < 3; ++s) bases[q * 7 + s] = -1;
 }
 
 __global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, int niso,
@@ -2513,6 +2533,7 @@ constexpr int kMaxRanks = 32;
 struct ExchangePeers {
   long long* gathered[kMaxRanks];            // each rank's gathered array (peer pointers)
   unsigned long long* flags[kMaxRanks];      // each rank's flags (peer pointers)
+  unsigned long long* slot_epoch[kMaxRanks]; // each rank's [2][world] epochs of the slots
 };
 
 __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
@@ -2538,11 +2559,22 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
   // used by odd and even epochs: a rank that finished waiting in epoch e may
   // still be reading half e % 2 when a faster peer writes epoch e + 1, and no
   // peer can reach epoch e + 2 before this rank has published e + 1.
-  const int64_t half = (int64_t)(ep & 1ull) * world * niso * 4;
+  //
+  // The two-half argument holds only while every wait succeeds.  So each
+  // slot also carries the epoch its totals belong to (slot_epoch, written
+  // before the flag is released): a rank whose wait ran out and that went on
+  // to later steps can get two epochs ahead of a slow peer and overwrite the
+  // half that peer reads; the peer then sees a slot epoch other than its own
+  // and records an error instead of planning from newer totals.  After any
+  // such error the exchange's state is not trusted: the engine (its
+  // exchange) is created again.
+  const int64_t hb = (int64_t)(ep & 1ull);
+  const int64_t half = hb * world * niso * 4;
   for (int r = lane; r < world; r += 32) {
     long long* dst = peers.gathered[r] + half + (int64_t)rank * niso * 4;
     for (int q = 0; q < niso; ++q)
       for (int t = 0; t < 4; ++t) dst[4 * q + t] = own_info[16 * q + t];
+    peers.slot_epoch[r][hb * world + rank] = ep;
   }
   __threadfence_system();
   __syncwarp();
@@ -2561,6 +2593,9 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
       __nanosleep(32);
     }
   }
+  // Every slot of the half must hold this epoch's totals.
+  for (int r = lane; r < world; r += 32)
+    if (ld_acquire_sys_u64(peers.slot_epoch[rank] + hb * world + r) != ep) ok = false;
   if (!__all_sync(0xffffffffu, ok) && lane == 0)
     atomicExch((unsigned long long*)err, (unsigned long long)TKMC_ERR_DEVICE_TIMEOUT);
   __syncwarp();
@@ -2978,12 +3013,19 @@ FeWsAll fe_views(const FeLayout& f, void* ws, int niso) {
 
 // Raise a kernel's dynamic shared memory limit once per device (and size),
 // so that launch sequences need no attribute calls (they may be captured
-// into CUDA graphs).
+// into CUDA graphs).  The limit only ever grows: the check, the attribute
+// call and the cached value change together under one lock, so two host
+// threads asking for different sizes cannot leave the attribute below the
+// cached value.  The cache is stored after the attribute is set, so a
+// thread that reads a large enough value without the lock may launch.
 template <typename F>
 int ensure_smem(F* kernel, size_t bytes, std::atomic<size_t>* per_device) {
+  static std::mutex mu;
   int dev = 0;
   TK_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return set_err(TKMC_ERR_CUDA, "device index %d out of range", dev);
+  if (per_device[dev].load() >= bytes) return TKMC_OK;
+  std::lock_guard<std::mutex> lock(mu);
   if (per_device[dev].load() >= bytes) return TKMC_OK;
   TK_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
   per_device[dev].store(bytes);
@@ -3055,6 +3097,26 @@ int noalloc_scratch_address(void** out) {
     cache[dev] = p;
   }
   *out = cache[dev];
+  return TKMC_OK;
+}
+
+// The end of a scan call: read the total and the look-back error word back
+// (one synchronisation).  With total == NULL the error word is still read,
+// so an expired look-back wait is reported either way, except while the
+// stream is being captured into a CUDA graph: nothing can be read then, and
+// the call returns after the launch.
+int scan_finish(const long long* info, int64_t* total, cudaStream_t st) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  TK_CUDA(cudaStreamIsCapturing(st, &cap));
+  if (cap != cudaStreamCaptureStatusNone) {
+    if (total) return set_err(TKMC_ERR_INVALID_ARG, "scan total cannot be read during stream capture");
+    return TKMC_OK;
+  }
+  long long h[3];
+  TK_CUDA(cudaMemcpyAsync(h, info, sizeof(h), cudaMemcpyDeviceToHost, st));
+  TK_CUDA(cudaStreamSynchronize(st));
+  if (h[2]) return set_err(TKMC_ERR_DEVICE_TIMEOUT, "scan look-back wait expired");
+  if (total) *total = h[1];
   return TKMC_OK;
 }
 
@@ -3184,14 +3246,7 @@ int tkmc_scan_i32(const int32_t* in, int32_t* out, int64_t n, int inclusive, voi
   k_scan_i32<<<(unsigned)tiles, kThreads, 0, st>>>(in, out, n, inclusive, flags, agg, incl, info,
                                                    g_wait_ns.load(), skip);
   TK_LAUNCHED();
-  if (total) {
-    long long h[3];
-    TK_CUDA(cudaMemcpyAsync(h, info, sizeof(h), cudaMemcpyDeviceToHost, st));
-    TK_CUDA(cudaStreamSynchronize(st));
-    if (h[2]) return set_err(TKMC_ERR_DEVICE_TIMEOUT, "scan look-back wait expired");
-    *total = h[1];
-  }
-  return TKMC_OK;
+  return scan_finish(info, total, st);
 }
 
 int tkmc_scan_i32_noalloc(const int32_t* in, int32_t* out, int64_t n, int inclusive,
@@ -3223,14 +3278,7 @@ int tkmc_scan_i32_noalloc(const int32_t* in, int32_t* out, int64_t n, int inclus
   k_scan_i32<<<(unsigned)tiles, kThreads, 0, st>>>(in, out, n, inclusive, flags, agg, incl, info,
                                                    g_wait_ns.load(), -1);
   TK_LAUNCHED();
-  if (total) {
-    long long h[3];
-    TK_CUDA(cudaMemcpyAsync(h, info, sizeof(h), cudaMemcpyDeviceToHost, st));
-    TK_CUDA(cudaStreamSynchronize(st));
-    if (h[2]) return set_err(TKMC_ERR_DEVICE_TIMEOUT, "scan look-back wait expired");
-    *total = h[1];
-  }
-  return TKMC_OK;
+  return scan_finish(info, total, st);
 }
 
 // ---- flying edges --------------------------------------------------------
@@ -3363,7 +3411,11 @@ int tkmc_fe_check(int64_t nx, int64_t ny, int64_t nz, int niso, void* ws, size_t
   for (int q = 0; q < niso; ++q) {
     const long long e = h[q * 16 + 10];
     if (e == TKMC_ERR_DEVICE_TIMEOUT)
-      return set_err((int)e, "a device wait expired: scan look-back or totals exchange (isovalue %d)", q);
+      return set_err((int)e, "a device wait expired, or a peer was out of step: scan look-back "
+                             "or totals exchange (isovalue %d)", q);
+    if (e == TKMC_ERR_OVERFLOW)
+      return set_err((int)e, "the global point total does not fit int32 point ids: nothing "
+                             "was emitted (isovalue %d)", q);
     if (e)
       return set_err((int)e, "fe emit wrote past the output capacity (isovalue %d)", q);
   }
@@ -3630,8 +3682,10 @@ int tkmc_fe_emit_batch(const float* const* vols, int64_t nblocks, int64_t nx, in
 
 struct tkmc_exchange_impl {
   int world, rank, niso, device;
-  char* base;  // one allocation: flags [world] u64 | gathered [2][world][niso][4] i64 | epoch u64
-  size_t off_gathered, off_epoch, bytes;
+  // one allocation: flags [world] u64 | gathered [2][world][niso][4] i64 |
+  // slot epochs [2][world] u64 | epoch u64
+  char* base;
+  size_t off_gathered, off_slot_epoch, off_epoch, bytes;
   ExchangePeers peers;
   void* opened[kMaxRanks];
 };
@@ -3649,7 +3703,8 @@ int tkmc_exchange_create(int world, int rank, int niso, void** out, void* handle
   x->niso = niso;
   cudaError_t e = cudaGetDevice(&x->device);
   x->off_gathered = align_up((size_t)world * 8, 256);
-  x->off_epoch = x->off_gathered + align_up((size_t)2 * world * niso * 4 * 8, 256);
+  x->off_slot_epoch = x->off_gathered + align_up((size_t)2 * world * niso * 4 * 8, 256);
+  x->off_epoch = x->off_slot_epoch + align_up((size_t)2 * world * 8, 256);
   x->bytes = x->off_epoch + 256;
   if (e == cudaSuccess) e = cudaMalloc(&x->base, x->bytes);
   if (e == cudaSuccess) e = cudaMemset(x->base, 0, x->bytes);
@@ -3679,6 +3734,7 @@ int tkmc_exchange_connect(void* xp, const void* handles) {
     }
     x->peers.flags[r] = reinterpret_cast<unsigned long long*>(b);
     x->peers.gathered[r] = reinterpret_cast<long long*>(b + x->off_gathered);
+    x->peers.slot_epoch[r] = reinterpret_cast<unsigned long long*>(b + x->off_slot_epoch);
   }
   return TKMC_OK;
 }
@@ -3693,6 +3749,7 @@ int tkmc_exchange_connect_local(void* xp, void* const* members) {
       return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_connect_local: member %d does not match", r);
     x->peers.flags[r] = reinterpret_cast<unsigned long long*>(m->base);
     x->peers.gathered[r] = reinterpret_cast<long long*>(m->base + m->off_gathered);
+    x->peers.slot_epoch[r] = reinterpret_cast<unsigned long long*>(m->base + m->off_slot_epoch);
   }
   return TKMC_OK;
 }

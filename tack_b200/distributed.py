@@ -4,9 +4,14 @@ The volume is split into contiguous runs of node planes.  Rank r owns node
 planes [p0, p1) and also holds plane p1 as a read-only ghost (except the last
 rank), so it can close its last layer of cells.  Each rank classifies,
 counts and scans its slab independently (tkmc_fe_count with ghost_plane=1);
-the only exchange is ONE all-gather of 4 int64 totals per isovalue per rank
-(NCCL over NVLink).  From the gathered totals every rank computes the global
-point-id bases of its x, y and z sections, then emits its points and
+the only exchange is one gather of 4 int64 totals per isovalue per rank.  By
+default (exchange="p2p") that is one small kernel that stores this rank's
+totals straight into every other rank's memory over NVLink (CUDA IPC
+mappings, epoch flags, bounded wait) and plans in the same launch; with
+exchange="nccl" it is an NCCL all-gather followed by a plan kernel.  The
+host-side run() uses an all-gather through the process group.  From the
+gathered totals every rank computes the global point-id bases of its x, y
+and z sections, then emits its points and
 triangles into rank-local buffers holding exactly its slices of the global
 output.  Point ids in conn are global, and the assembled output is
 byte-identical to a single-volume flying_edges call: seams are merged, not

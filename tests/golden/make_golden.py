@@ -2,11 +2,12 @@
 
 Runs berkgeveci/tack's own code on its CPU backend (tack.cpu, llvmlite JIT)
 and records inputs and outputs as .npz files.  The reference is imported
-from a source checkout given by ``--reference`` (default ``/root/reference``,
-read-only; nothing is written there).  The fixtures are committed; the tests
-never need the reference itself.
+from a source checkout of berkgeveci/tack given by ``--reference`` or, when
+that is omitted, by the environment variable TACK_REFERENCE (read-only;
+nothing is written there).  The fixtures are committed; the tests never need
+the reference itself.
 
-    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py
+    PYTHONDONTWRITEBYTECODE=1 python tests/golden/make_golden.py --reference <checkout>
 
 What is recorded (all through the reference's public or module-level API):
   mc_tables.npz     _TRI_TABLE, _NUM_TRIS, _EDGE_CORNERS (flying_edges.py:33-306)
@@ -340,9 +341,12 @@ def run_normals(tack, out_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TACK_REFERENCE"),
+                    help="source checkout of berkgeveci/tack (default: $TACK_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give the reference checkout with --reference or TACK_REFERENCE")
     tack = load_reference(a.reference)
     fe_mod = importlib.import_module("tack.algorithms.flying_edges")
     np.savez_compressed(os.path.join(a.out, "mc_tables.npz"), tri_table=fe_mod._TRI_TABLE,

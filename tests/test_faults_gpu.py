@@ -102,3 +102,79 @@ def test_exchange_wait_expires_with_status(tack, short_wait):
             lib.tkmc_exchange_destroy(x)
     got = capi_fe(c["values"], c["grid_tuple"], [0.0])
     np.testing.assert_array_equal(got["conn"], c["conn"])
+
+
+def test_scan_timeout_reported_without_total(tack, short_wait):
+    """With total == NULL the scan still reads its look-back error word back,
+    so an expired wait is reported."""
+    lib = short_wait
+    n = 5 * 4096 + 17
+    a = torch.ones(n, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(a)
+    nb = lib.tkmc_scan_workspace_bytes(n)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    lib.tkmc_test_skip_publish(3)
+    rc = lib.tkmc_scan_i32(a.data_ptr(), out.data_ptr(), n, 0, ws.data_ptr(), nb, None, stream())
+    assert rc == _lib.TKMC_ERR_DEVICE_TIMEOUT
+    assert lib.tkmc_scan_i32(a.data_ptr(), out.data_ptr(), n, 1, ws.data_ptr(), nb, None,
+                             stream()) == 0
+    assert torch.equal(out.cpu(), torch.arange(1, n + 1, dtype=torch.int32))
+
+
+@pytest.mark.parametrize("shape", ["unaligned", "aligned"])
+def test_device_plan_refuses_point_ids_beyond_int32(tack, shape):
+    """Device-side planning from gathered totals whose global point count
+    exceeds INT32_MAX: the plan marks the bases, every emit kernel then writes
+    nothing and records TKMC_ERR_OVERFLOW, which tkmc_fe_check returns.
+    The totals of the other rank are faked (2^31 points); this rank's own
+    slab is a real volume (rows of 49 nodes: the word-granular emit; rows of
+    64 nodes: the unit-driven emit)."""
+    import ctypes
+    from tack_b200 import workloads
+    lib = _lib.load()
+    if shape == "unaligned":
+        c = load_fe_case("gyroid48")
+        nx, ny, nz = c["grid_tuple"][:3]
+        v = torch.from_numpy(c["values"]).cuda()
+        iso = 0.0
+    else:
+        nx = ny = nz = 63
+        v = workloads.generate("sphere")
+        iso = 0.0
+    nb = lib.tkmc_fe_workspace_bytes(nx, ny, nz, 1)
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    counts = np.zeros(4, np.int64)
+    _lib.check(lib.tkmc_fe_count(v.data_ptr(), nx, ny, nz, 0, f32arr([iso]), 1, None,
+                                 ws.data_ptr(), nb, counts.ctypes.data, stream()), "count")
+    assert counts[:3].sum() > 0 and counts[3] > 0
+    # Rank 0 (this slab) and a faked rank 1 whose x section alone holds 2^31 points.
+    allc = torch.tensor(np.concatenate([counts, [1 << 31, 0, 0, 0]]), dtype=torch.int64,
+                        device="cuda")
+    bases = torch.zeros(7, dtype=torch.int64, device="cuda")
+    _lib.check(lib.tkmc_fe_plan(allc.data_ptr(), 2, 0, 1, 0, bases.data_ptr(), stream()), "plan")
+    P, T = int(counts[:3].sum()), int(counts[3])
+    pts = torch.full((P * 3,), 7.0, dtype=torch.float32, device="cuda")
+    conn = torch.full((T * 3,), -7, dtype=torch.int32, device="cuda")
+    geom = f32arr([0.0, 0.0, 0.0, 1.0, 1.0, 1.0])
+    _lib.check(lib.tkmc_fe_emit_dev(v.data_ptr(), nx, ny, nz, 0, 0, geom, f32arr([iso]), 1, None,
+                                    ws.data_ptr(), nb, bases.data_ptr(), pts.data_ptr(), P,
+                                    conn.data_ptr(), T, stream()), "emit_dev")
+    rc = lib.tkmc_fe_check(nx, ny, nz, 1, ws.data_ptr(), nb, stream())
+    assert rc == _lib.TKMC_ERR_OVERFLOW
+    assert b"int32 point ids" in lib.tkmc_last_error()
+    assert bool((pts == 7.0).all()) and bool((conn == -7).all())
+    # Totals that fit (rank 1 with triangles only, so this rank's point ids
+    # are those of the volume alone): the same calls emit the single-volume
+    # connectivity.
+    allc_ok = torch.tensor(np.concatenate([counts, [0, 0, 0, 5]]), dtype=torch.int64,
+                           device="cuda")
+    _lib.check(lib.tkmc_fe_count(v.data_ptr(), nx, ny, nz, 0, f32arr([iso]), 1, None,
+                                 ws.data_ptr(), nb, counts.ctypes.data, stream()), "count")
+    _lib.check(lib.tkmc_fe_plan(allc_ok.data_ptr(), 2, 0, 1, 0, bases.data_ptr(), stream()),
+               "plan")
+    _lib.check(lib.tkmc_fe_emit_dev(v.data_ptr(), nx, ny, nz, 0, 0, geom, f32arr([iso]), 1, None,
+                                    ws.data_ptr(), nb, bases.data_ptr(), pts.data_ptr(), P,
+                                    conn.data_ptr(), T, stream()), "emit_dev")
+    _lib.check(lib.tkmc_fe_check(nx, ny, nz, 1, ws.data_ptr(), nb, stream()), "check")
+    got = capi_fe(v, (nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0), [iso])
+    np.testing.assert_array_equal(conn.cpu().numpy().reshape(-1, 3), got["conn"])

@@ -5,9 +5,11 @@ inside a simulation's time step, on a GPU whose memory the simulation has
 reserved, where cudaMalloc would fail or synchronise the device.  For them
 the library keeps the scan's scratch in a static device array.  This checks,
 through the C ABI, that two calls in a row give exactly what the
-workspace-taking tkmc_scan_i32 gives (integer results: bit-exact), and that
-sizes beyond the array's limit are refused.  This file is collected last so
-that a failure here leaves every other test already run.
+workspace-taking tkmc_scan_i32 gives and exactly the int32 prefix sums
+computed on the host with numpy (int64 cumsum wrapped to int32, as the
+reference's int32 fields wrap; integer results: bit-exact), and that sizes
+beyond the array's limit are refused.  This file is collected last so that a
+failure here leaves every other test already run.
 """
 
 import ctypes
@@ -32,14 +34,21 @@ def _scan_with_workspace(lib, x, inclusive):
     return out, tot.value
 
 
-def _scan_noalloc(lib, x, inclusive):
+def _scan_noalloc(lib, x, inclusive, want_total=True):
     out = torch.full_like(x, -1)
     tot = ctypes.c_int64(0)
     _lib.check(lib.tkmc_scan_i32_noalloc(x.data_ptr(), out.data_ptr(), x.numel(), inclusive,
-                                         ctypes.byref(tot),
+                                         ctypes.byref(tot) if want_total else None,
                                          torch.cuda.current_stream().cuda_stream),
                "tkmc_scan_i32_noalloc")
     return out, tot.value
+
+
+def _scan_host(a, inclusive):
+    """Exact prefix sums on the host: int64 cumsum, stored as wrapped int32."""
+    c = np.cumsum(a.astype(np.int64))
+    ex = c if inclusive else np.concatenate([[0], c[:-1]])
+    return ex.astype(np.int32), int(c[-1])
 
 
 def test_noalloc_scan_matches_workspace_scan_on_consecutive_calls():
@@ -50,11 +59,31 @@ def test_noalloc_scan_matches_workspace_scan_on_consecutive_calls():
     # the shared static scratch.
     cases = [(3_000_017, 0, (-40, 900)), (70_001, 1, (0, 7))]
     for n, inclusive, (lo, hi) in cases:
-        x = torch.from_numpy(rng.integers(lo, hi, n).astype(np.int32)).cuda()
+        a = rng.integers(lo, hi, n).astype(np.int32)
+        x = torch.from_numpy(a).cuda()
         ref, ref_total = _scan_with_workspace(lib, x, inclusive)
         got, got_total = _scan_noalloc(lib, x, inclusive)
-        assert got_total == ref_total
+        host, host_total = _scan_host(a, inclusive)
+        assert got_total == ref_total == host_total
         assert torch.equal(got, ref)
+        assert np.array_equal(got.cpu().numpy(), host)
+
+
+def test_noalloc_scan_wraps_int32_and_runs_without_total():
+    """Values whose running sum passes INT32_MAX wrap exactly as int32 fields
+    do, the total stays exact in int64, and a call without a total pointer
+    still returns the same prefix sums (it checks the look-back error word
+    itself)."""
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    a = np.full(1_200_000, 2_000, np.int32)  # running sum reaches 2.4e9
+    x = torch.from_numpy(a).cuda()
+    host, host_total = _scan_host(a, 0)
+    got, got_total = _scan_noalloc(lib, x, 0)
+    assert got_total == host_total == 2_400_000_000
+    assert np.array_equal(got.cpu().numpy(), host)
+    got2, _ = _scan_noalloc(lib, x, 1, want_total=False)
+    assert np.array_equal(got2.cpu().numpy(), _scan_host(a, 1)[0])
 
 
 def test_noalloc_scan_refuses_sizes_beyond_its_limit():
