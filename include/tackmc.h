@@ -300,6 +300,16 @@ int tkmc_exchange_plan(void* exchange, int64_t nx, int64_t ny, int64_t nz,
                        int ghost_plane, const void* workspace, size_t workspace_bytes,
                        int shared_output, int64_t* bases_dev, void* stream);
 int tkmc_exchange_destroy(void* exchange);
+/* tkmc_exchange_plan right after the count pass (tkmc_fe_scan_part part 1):
+ * this rank's totals are summed from the count pass's tile totals, so the
+ * exchange -- peer stores, the wait for the slowest rank, the plan -- can
+ * run on a second stream while the offsets pass (part 2) runs on the first;
+ * the emit then waits for both.  Same arguments and results as
+ * tkmc_exchange_plan.  No counterpart in the reference. */
+int tkmc_exchange_plan_counts(void* exchange, int64_t nx, int64_t ny, int64_t nz,
+                              int ghost_plane, const void* workspace,
+                              size_t workspace_bytes, int shared_output,
+                              int64_t* bases_dev, void* stream);
 
 /* Copy the device status word of each isovalue (niso int64: 0, or the
  * TKMC_ERR_* code the last count/emit recorded -- TKMC_ERR_DEVICE_TIMEOUT,
@@ -342,13 +352,22 @@ int tkmc_fe_check(int64_t nx, int64_t ny, int64_t nz, int niso,
  * phases.  classify = one volume read -> node bitmasks (asynchronous);
  * scan = counts + offsets from the bitmasks (asynchronous);
  * read_counts = copy counts to HOST and check the device error word
- * (synchronises).  classify + scan + read_counts == tkmc_fe_count. */
+ * (synchronises).  classify + scan + read_counts == tkmc_fe_count.
+ * scan_part splits scan in two: part 1 = the count pass (the per-row
+ * counts and the totals; on rows whose length is a multiple of 32 nodes,
+ * only the counts and their tile totals), part 2 = the offsets pass (the
+ * per-row offsets and the output units; nothing on other rows).  Part 1
+ * then part 2 == scan; between them tkmc_exchange_plan_counts may run on
+ * another stream. */
 int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
                      const float* isovalues, int niso, void* workspace,
                      size_t workspace_bytes, void* stream);
 int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
                  int niso, const int32_t* mask, void* workspace,
                  size_t workspace_bytes, void* stream);
+int tkmc_fe_scan_part(int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                      int niso, const int32_t* mask, void* workspace,
+                      size_t workspace_bytes, int part, void* stream);
 int tkmc_fe_read_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
                         void* workspace, size_t workspace_bytes,
                         int64_t* counts, void* stream);

@@ -54,6 +54,7 @@ SIGNATURES = {
     "tkmc_exchange_connect_local": (_I, [_P, _P]),
     "tkmc_exchange_plan": (_I, [_P, _I64, _I64, _I64, _I, _P, _SZ, _I, _P, _P]),
     "tkmc_exchange_destroy": (_I, [_P]),
+    "tkmc_exchange_plan_counts": (_I, [_P, _I64, _I64, _I64, _I, _P, _SZ, _I, _P, _P]),
     "tkmc_fe_emit_soup": (_I, [_P, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _P, _P, _P,
                                _I64, _P]),
     "tkmc_fe_plan": (_I, [_P, _I, _I, _I, _I, _P, _P]),
@@ -64,6 +65,7 @@ SIGNATURES = {
     "tkmc_fe_check": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P]),
     "tkmc_fe_classify": (_I, [_P, _I64, _I64, _I64, _P, _I, _P, _SZ, _P]),
     "tkmc_fe_scan": (_I, [_I64, _I64, _I64, _I, _I, _P, _P, _SZ, _P]),
+    "tkmc_fe_scan_part": (_I, [_I64, _I64, _I64, _I, _I, _P, _P, _SZ, _I, _P]),
     "tkmc_fe_read_counts": (_I, [_I64, _I64, _I64, _I, _P, _SZ, _P, _P]),
     "tkmc_fe_row_offsets": (_I, [_I64, _I64, _I64, _I, _I, _P, _SZ, _P, _P]),
     "tkmc_fe_run": (_I, [_P, _I64, _I64, _I64, _P, _P, _I, _P, _P, _SZ, _P, _I64, _P, _I64,

@@ -2545,13 +2545,59 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned 
   return v;
 }
 
+// This slab's own totals {X, Y, Z, T} of isovalue q from the count pass
+// alone (word-aligned rows, right after K2a): the super-tile totals of the
+// whole super-tiles of own rows, the tile totals of the rest of the whole
+// tiles, and the row counts of the last partial tile.  Called by one warp;
+// every lane returns the sums.
+__device__ void own_totals_from_counts(const FeDims& d, const FeIsoWs& W, long long (&out)[4]) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n = d.n_own_rows;
+  const int64_t tiles = n / kThreads, supers = tiles / kSuperTiles;
+  long long a[4] = {0, 0, 0, 0};
+  for (int64_t i = lane; i < supers; i += 32)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) a[t] += __ldcg(W.super + i * 5 + t);
+  for (int64_t i = supers * kSuperTiles + lane; i < tiles; i += 32)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) a[t] += __ldcg(W.agg + i * 5 + t);
+  for (int64_t r = tiles * kThreads + lane; r < n; r += 32) {
+    const int4 c = __ldcg(reinterpret_cast<const int4*>(W.cnt) + r);
+    a[0] += c.x;
+    a[1] += c.y;
+    a[2] += c.z;
+    a[3] += c.w;
+  }
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a[t] += __shfl_xor_sync(0xffffffffu, a[t], o);
+    out[t] = a[t];
+  }
+}
+
+// from_counts: this rank's totals come from the count pass's tile totals
+// (own_totals_from_counts), so the exchange can run as soon as K2a is done,
+// concurrently with K2b on another stream; else from the info words the
+// offsets pass (or the row scan) wrote.
 __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoch, int world,
                                    int rank, int niso, const long long* __restrict__ own_info,
-                                   int shared_output, long long* __restrict__ bases,
-                                   long long* err, int64_t wait_ns) {
+                                   int from_counts, FeDims d, FeWsAll ws, int shared_output,
+                                   long long* __restrict__ bases, long long* err,
+                                   int64_t wait_ns) {
   const int lane = threadIdx.x;  // one warp
   __shared__ unsigned long long s_epoch;
+  __shared__ long long s_own[TKMC_MAX_ISO][4];
   if (lane == 0) s_epoch = ++(*epoch);
+  for (int q = 0; q < niso; ++q) {
+    if (from_counts) {
+      long long o[4];
+      own_totals_from_counts(d, ws.iso[q], o);
+      if (lane < 4) s_own[q][lane] = o[lane];
+    } else if (lane < 4) {
+      s_own[q][lane] = own_info[16 * q + lane];
+    }
+  }
   __syncwarp();
   const unsigned long long ep = s_epoch;
   // This rank's totals {X, Y, Z, T} per isovalue (info[16 q + 0..3]) into
@@ -2573,7 +2619,7 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
   for (int r = lane; r < world; r += 32) {
     long long* dst = peers.gathered[r] + half + (int64_t)rank * niso * 4;
     for (int q = 0; q < niso; ++q)
-      for (int t = 0; t < 4; ++t) dst[4 * q + t] = own_info[16 * q + t];
+      for (int t = 0; t < 4; ++t) dst[4 * q + t] = s_own[q][t];
     peers.slot_epoch[r][hb * world + rank] = ep;
   }
   __threadfence_system();
@@ -3326,8 +3372,12 @@ int tkmc_fe_classify(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   return TKMC_OK;
 }
 
-int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
-                 const int32_t* mask, void* ws, size_t ws_bytes, void* stream) {
+// parts: 1 = the count pass (word-aligned rows: K2a; other rows: the whole
+// count and row scan), 2 = the offsets pass (word-aligned rows: K2b; other
+// rows: nothing), 3 = both.
+static int fe_scan_impl(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
+                        const int32_t* mask, void* ws, size_t ws_bytes, int parts,
+                        void* stream) {
   FeLayout f;
   if (!fe_layout(nx, ny, nz, ghost_plane, niso, &f))
     return set_err(TKMC_ERR_INVALID_ARG, "bad grid or niso");
@@ -3335,14 +3385,25 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
   if (rc) return rc;
   FeWsAll v = fe_views(f, ws, niso);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool aligned = (f.d.L & 31) == 0;
+  if (!(parts & 1)) {
+    if (aligned) {
+      k_fe_offsets_units<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
+          f.d, v, f.unit_cap, 0);
+      TK_LAUNCHED();
+    }
+    return TKMC_OK;
+  }
   TK_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + f.off_info, 0, f.reset_bytes - f.off_info, st));
   const int64_t skip = g_skip_tile.exchange(-1);
-  if ((f.d.L & 31) == 0) {  // no waits between blocks here: the skip hook does not apply
+  if (aligned) {  // no waits between blocks here: the skip hook does not apply
     const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
     k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
     TK_LAUNCHED();
-    k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, f.unit_cap, 0);
-    TK_LAUNCHED();
+    if (parts & 2) {
+      k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, f.unit_cap, 0);
+      TK_LAUNCHED();
+    }
     return TKMC_OK;
   }
   if (f.k2_smem > 48 * 1024)
@@ -3354,6 +3415,18 @@ int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
       f.d, v, g_wait_ns.load(), skip);
   TK_LAUNCHED();
   return TKMC_OK;
+}
+
+int tkmc_fe_scan(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
+                 const int32_t* mask, void* ws, size_t ws_bytes, void* stream) {
+  return fe_scan_impl(nx, ny, nz, ghost_plane, niso, mask, ws, ws_bytes, 3, stream);
+}
+
+int tkmc_fe_scan_part(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int niso,
+                      const int32_t* mask, void* ws, size_t ws_bytes, int part, void* stream) {
+  if (part != 1 && part != 2)
+    return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_scan_part: part must be 1 or 2, got %d", part);
+  return fe_scan_impl(nx, ny, nz, ghost_plane, niso, mask, ws, ws_bytes, part, stream);
 }
 
 int tkmc_fe_read_counts(int64_t nx, int64_t ny, int64_t nz, int niso, void* ws, size_t ws_bytes,
@@ -3754,9 +3827,9 @@ int tkmc_exchange_connect_local(void* xp, void* const* members) {
   return TKMC_OK;
 }
 
-int tkmc_exchange_plan(void* xp, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
-                       const void* ws, size_t ws_bytes, int shared_output, int64_t* bases_dev,
-                       void* stream) {
+static int exchange_plan_impl(void* xp, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                              const void* ws, size_t ws_bytes, int shared_output,
+                              int64_t* bases_dev, int after_count_pass, void* stream) {
   tkmc_exchange_impl* x = static_cast<tkmc_exchange_impl*>(xp);
   if (!x || !bases_dev) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_exchange_plan: NULL argument");
   FeLayout f;
@@ -3765,12 +3838,30 @@ int tkmc_exchange_plan(void* xp, int64_t nx, int64_t ny, int64_t nz, int ghost_p
   int rc = check_ws(const_cast<void*>(ws), ws_bytes, f.total);
   if (rc) return rc;
   const long long* info = reinterpret_cast<const long long*>(static_cast<const char*>(ws) + f.off_info);
+  // Word-aligned rows keep tile totals after the count pass; other rows
+  // finish their totals in the count pass itself (the row scan).
+  const int from_counts = after_count_pass && (f.d.L & 31) == 0;
   k_fe_exchange_plan<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
       x->peers, reinterpret_cast<unsigned long long*>(x->base + x->off_epoch), x->world, x->rank,
-      x->niso, info, shared_output, reinterpret_cast<long long*>(bases_dev),
-      const_cast<long long*>(info) + 10, g_wait_ns.load());
+      x->niso, info, from_counts, f.d, fe_views(f, const_cast<void*>(ws), x->niso), shared_output,
+      reinterpret_cast<long long*>(bases_dev), const_cast<long long*>(info) + 10,
+      g_wait_ns.load());
   TK_LAUNCHED();
   return TKMC_OK;
+}
+
+int tkmc_exchange_plan(void* xp, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                       const void* ws, size_t ws_bytes, int shared_output, int64_t* bases_dev,
+                       void* stream) {
+  return exchange_plan_impl(xp, nx, ny, nz, ghost_plane, ws, ws_bytes, shared_output, bases_dev,
+                            0, stream);
+}
+
+int tkmc_exchange_plan_counts(void* xp, int64_t nx, int64_t ny, int64_t nz, int ghost_plane,
+                              const void* ws, size_t ws_bytes, int shared_output,
+                              int64_t* bases_dev, void* stream) {
+  return exchange_plan_impl(xp, nx, ny, nz, ghost_plane, ws, ws_bytes, shared_output, bases_dev,
+                            1, stream);
 }
 
 int tkmc_exchange_destroy(void* xp) {

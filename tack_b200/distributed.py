@@ -179,7 +179,9 @@ class SlabEngine:
         # Device-side plan: this rank's totals and its output bases.
         self.counts_dev = torch.zeros(len(self.isos) * 4, dtype=torch.int64, device=self.dev)
         self.bases_dev = torch.zeros(len(self.isos) * 7, dtype=torch.int64, device=self.dev)
+        self._xstream = None
         if exchange == "p2p" and world > 1:
+            self._xstream = torch.cuda.Stream(self.dev)
             self._connect_p2p()
 
     def _connect_p2p(self):
@@ -256,15 +258,21 @@ class SlabEngine:
         return pts[:own_p * 3], conn[:own_t * 3]
 
     def run_device(self, local_values, points, conn, counts_host=None, marks=None):
-        """count -> totals all-gather (NCCL, device buffers) -> plan -> emit,
-        with nothing read on the host in between.  points / conn are flat
-        f32 / int32 CUDA tensors whose sizes are the capacities; writes past
-        them are skipped and reported by check().  When counts_host (pinned
-        int64, niso*4) is given, this rank's totals are copied there
-        asynchronously.  Every rank takes the same collective (or peer
-        exchange) each call.
-        marks: optional 5 CUDA events, recorded before the classify, scan,
-        plan and emit phases and after the emit (phase timing)."""
+        """classify -> count -> totals exchange and plan -> emit, with nothing
+        read on the host in between.  With the peer exchange the count pass
+        is split: the exchange kernel runs on a second stream right after
+        the per-row counts, while the offsets pass runs on this one, and the
+        emit waits for both.  Otherwise: the offsets pass, the totals copied
+        to a device array (with several ranks, NCCL-all-gathered), a plan
+        kernel.  points / conn
+        are flat f32 / int32 CUDA tensors whose sizes are the capacities;
+        writes past them are skipped and reported by check().  When
+        counts_host (pinned int64, niso*4) is given, this rank's totals are
+        copied there asynchronously.  Every rank takes the same collective
+        (or peer exchange) each call.
+        marks: optional 5 CUDA events, recorded before the classify, the
+        count, after the offsets pass, when the bases are ready (the wait
+        for the exchange) and after the emit (phase timing)."""
         import torch.distributed as dist
         g, p, lib = self.grid, self.plan, self.lib
         niso = len(self.isos)
@@ -281,15 +289,30 @@ class SlabEngine:
                                         niso, self.ws.data_ptr(), self.nbytes, st),
                    "tkmc_fe_classify")
         mark(1)
-        _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, p.nz_cells, ghost, niso, None,
-                                    self.ws.data_ptr(), self.nbytes, st), "tkmc_fe_scan")
-        mark(2)
-        if self._xchg is not None:  # totals over NVLink peer stores, plan in the same kernel
-            _lib.check(lib.tkmc_exchange_plan(self._xchg, g.nx, g.ny, p.nz_cells, ghost,
-                                              self.ws.data_ptr(), self.nbytes, 0,
-                                              self.bases_dev.data_ptr(), st),
-                       "tkmc_exchange_plan")
+        bases = self.bases_dev.data_ptr()
+        if self._xchg is not None:
+            # Totals over NVLink peer stores, plan in the same kernel, on a
+            # second stream as soon as the count pass is done: the exchange
+            # (and the wait for the slowest rank) overlaps the offsets pass.
+            _lib.check(lib.tkmc_fe_scan_part(g.nx, g.ny, p.nz_cells, ghost, niso, None,
+                                             self.ws.data_ptr(), self.nbytes, 1, st),
+                       "tkmc_fe_scan_part")
+            main = torch.cuda.current_stream(self.dev)
+            self._xstream.wait_stream(main)
+            _lib.check(lib.tkmc_exchange_plan_counts(self._xchg, g.nx, g.ny, p.nz_cells, ghost,
+                                                     self.ws.data_ptr(), self.nbytes, 0, bases,
+                                                     self._xstream.cuda_stream),
+                       "tkmc_exchange_plan_counts")
+            _lib.check(lib.tkmc_fe_scan_part(g.nx, g.ny, p.nz_cells, ghost, niso, None,
+                                             self.ws.data_ptr(), self.nbytes, 2, st),
+                       "tkmc_fe_scan_part")
+            mark(2)
+            main.wait_stream(self._xstream)
         else:
+            _lib.check(lib.tkmc_fe_scan(g.nx, g.ny, p.nz_cells, ghost, niso, None,
+                                        self.ws.data_ptr(), self.nbytes, st), "tkmc_fe_scan")
+            mark(2)
+        if self._xchg is None:
             _lib.check(lib.tkmc_fe_copy_counts(g.nx, g.ny, p.nz_cells, niso, self.ws.data_ptr(),
                                                self.nbytes, self.counts_dev.data_ptr(), st),
                        "tkmc_fe_copy_counts")
@@ -297,13 +320,13 @@ class SlabEngine:
             if p.world > 1:
                 dist.all_gather_into_tensor(self.gathered, self.counts_dev, group=self.group)
                 src = self.gathered
-            _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso, 0,
-                                        self.bases_dev.data_ptr(), st), "tkmc_fe_plan")
+            _lib.check(lib.tkmc_fe_plan(src.data_ptr(), p.world, p.rank, niso, 0, bases, st),
+                       "tkmc_fe_plan")
         mark(3)
         _lib.check(lib.tkmc_fe_emit_dev(
             local_values.data_ptr(), g.nx, g.ny, p.nz_cells, ghost, p.k0,
             _f32([g.x0, g.y0, g.z0, g.dx, g.dy, g.dz]), isos, niso, None, self.ws.data_ptr(),
-            self.nbytes, self.bases_dev.data_ptr(), points.data_ptr(), points.numel() // 3,
+            self.nbytes, bases, points.data_ptr(), points.numel() // 3,
             conn.data_ptr(), conn.numel() // 3, st), "tkmc_fe_emit_dev")
         mark(4)
         if counts_host is not None:

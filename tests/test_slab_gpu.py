@@ -280,3 +280,78 @@ def test_shared_output_plan_single_gpu_parts(tack, oracle):
                                                        g.dz), isos)
     np.testing.assert_array_equal(cn.cpu().numpy().reshape(-1, 3), ref["conn"])
     assert_points_identical(pts.cpu().numpy().reshape(-1, 3), ref["points"])
+
+
+@pytest.mark.parametrize("cells", [(127, 70, 41), (95, 70, 41), (255, 300, 9),
+                                   (127, 255, 200)])
+def test_exchange_after_count_pass_plans_like_host(tack, cells):
+    """The peer exchange launched right after the count pass (its totals
+    summed from the tile totals and the row counts of a partial tile, since
+    the ghost plane's rows are excluded) plans the same bases as the host
+    from the full count, while the offsets pass runs on the main stream;
+    then the emit equals the host-planned emit.  One rank (world 1), so the
+    exchange waits only for itself; rows of 128 and 256 nodes take the
+    tile-total path, rows of 96 nodes the row-scan path."""
+    import ctypes
+    from tack_b200 import _lib
+    from tack_b200.distributed import SlabEngine, SlabPlan, slab_bases
+    from fe_helpers import f32arr, stream
+    lib = _lib.load()
+    nx, ny, nz = cells
+    rng = np.random.default_rng(nx + ny)
+    z, y, x = np.meshgrid(np.arange(nz + 1), np.arange(ny + 1), np.arange(nx + 1), indexing="ij")
+    v = (np.sin(x * 0.11) * np.cos(y * 0.07) + np.sin(z * 0.3 + 0.2)
+         + 0.1 * rng.standard_normal(x.shape)).astype(np.float32).reshape(-1)
+    vol = torch.from_numpy(v).cuda()
+    g = tack.UniformGrid(nx, ny, nz, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+    isos = [0.0, 0.5, -0.6]
+    niso = len(isos)
+    plane = (nx + 1) * (ny + 1)
+    # Rank 0 of a two-way split: its slab has a ghost plane.
+    p = SlabPlan(nz + 1, 2, 0)
+    e = SlabEngine(g, p, isos)
+    sv = vol[p.k0 * plane:p.k1 * plane]
+    counts = e.count(sv)
+    want_p, want_c = e.emit(sv, counts, slab_bases(counts[None], 0))
+    x = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(lib.tkmc_exchange_handle_bytes())
+    _lib.check(lib.tkmc_exchange_create(1, 0, niso, ctypes.byref(x), handle), "create")
+    try:
+        members = (ctypes.c_void_p * 1)(x.value)
+        _lib.check(lib.tkmc_exchange_connect_local(x, members), "connect_local")
+        bases = torch.full((niso * 7,), -5, dtype=torch.int64, device="cuda")
+        side = torch.cuda.Stream()
+        main = torch.cuda.current_stream()
+        for _ in range(2):  # two epochs
+            bases.fill_(-5)
+            _lib.check(lib.tkmc_fe_classify(sv.data_ptr(), nx, ny, p.nz_cells, f32arr(isos), niso,
+                                            e.ws.data_ptr(), e.nbytes, stream()), "classify")
+            _lib.check(lib.tkmc_fe_scan_part(nx, ny, p.nz_cells, 1, niso, None, e.ws.data_ptr(),
+                                             e.nbytes, 1, stream()), "scan part 1")
+            side.wait_stream(main)
+            _lib.check(lib.tkmc_exchange_plan_counts(x, nx, ny, p.nz_cells, 1, e.ws.data_ptr(),
+                                                     e.nbytes, 0, bases.data_ptr(),
+                                                     side.cuda_stream), "plan_counts")
+            _lib.check(lib.tkmc_fe_scan_part(nx, ny, p.nz_cells, 1, niso, None, e.ws.data_ptr(),
+                                             e.nbytes, 2, stream()), "scan part 2")
+            main.wait_stream(side)
+            b = slab_bases(counts[None], 0)
+            host_b = np.concatenate([b["id_base"], b["out_base"], b["tri_out"][:, None]], axis=1)
+            np.testing.assert_array_equal(bases.cpu().numpy().reshape(niso, 7), host_b)
+            P, T = int(counts[:, :3].sum()), int(counts[:, 3].sum())
+            pts = torch.empty(3 * P, dtype=torch.float32, device="cuda")
+            cn = torch.empty(3 * T, dtype=torch.int32, device="cuda")
+            _lib.check(lib.tkmc_fe_emit_dev(sv.data_ptr(), nx, ny, p.nz_cells, 1, p.k0,
+                                            f32arr([0, 0, 0, 1, 1, 1]), f32arr(isos), niso, None,
+                                            e.ws.data_ptr(), e.nbytes, bases.data_ptr(),
+                                            pts.data_ptr(), P, cn.data_ptr(), T, stream()),
+                       "emit_dev")
+            _lib.check(lib.tkmc_fe_check(nx, ny, p.nz_cells, niso, e.ws.data_ptr(), e.nbytes,
+                                         stream()), "check")
+            assert torch.equal(pts.view(torch.int32), want_p.view(torch.int32))
+            assert torch.equal(cn, want_c)
+        assert lib.tkmc_fe_scan_part(nx, ny, p.nz_cells, 1, niso, None, e.ws.data_ptr(), e.nbytes,
+                                     3, stream()) == _lib.TKMC_ERR_INVALID_ARG
+    finally:
+        torch.cuda.synchronize()
+        lib.tkmc_exchange_destroy(x)
