@@ -2105,7 +2105,8 @@ k_fe_emit_words(FeDims d, FeWsAll ws, FeEmitArgs A) {
 // offset of word w's first crossing there).  Then lane = point over all the
 // units' own crossings (two volume reads each, the reference's arithmetic),
 // and lane = cell over all their cut cells (case from the bits, triangle
-// slots by a per-unit segmented prefix, ids = group offset + rank of the
+// slots by a prefix over the task's cut cells -- consecutive units'
+// triangles are consecutive in conn -- ids = group offset + rank of the
 // crossing in its word).
 
 // Index of the first unit of node row `row` at word >= w.
@@ -2140,7 +2141,6 @@ __global__ void __launch_bounds__(kThreads, 4)
 k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
   __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
-  __shared__ long long s_tri[kThreads / 32][32];
   const int isoi = blockIdx.y;
   const FeIsoWs W = iso_ws(ws, isoi);
   const float* __restrict__ vol = block_vol(ws, A.v);
@@ -2152,7 +2152,6 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __syncthreads();
   const long long n_own = *((volatile long long*)(W.info + 12));
   uint32_t* U = s_rec[warp];
-  long long* TR = s_tri[warp];
   const int Wd = d.W, Li = (int)d.L;
   const int64_t L = d.L, plane = d.L * d.M;
   const uint32_t M32 = (uint32_t)d.M;
@@ -2176,6 +2175,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
     // ---- lane = unit ----
     const int64_t u = lane < G ? grp * G + lane : n_own;
     unsigned np = 0, nc = 0;
+    long long task_tri = 0;  // lane 0: the task's first triangle row
     uint32_t* rec = U + lane * kUS;
     if (u < n_own) {
       const uint4* up = reinterpret_cast<const uint4*>(W.units + u);
@@ -2234,7 +2234,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
       rec[kUCrd + 1] = __float_as_uint(coord(y0, (int64_t)q.j + 1, hy));
       rec[kUCrd + 2] = __float_as_uint(coord(z0, (int64_t)q.k + A.k_offset, hz));
       rec[kUCrd + 3] = __float_as_uint(coord(z0, (int64_t)q.k + 1 + A.k_offset, hz));
-      TR[lane] = outT + (long long)(((unsigned long long)u1.w << 32) | u1.z);
+      task_tri = outT + (long long)(((unsigned long long)u1.w << 32) | u1.z);
       np = __popc(m0) + __popc(m1) + __popc(m2);
       nc = __popc(act);
     }
@@ -2295,6 +2295,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
     }
 
     // ---- lane = cut cell ----
+    long long tcarry = __shfl_sync(0xffffffffu, task_tri, 0);
     for (unsigned c0 = 0; c0 < NC; c0 += 32) {
       const unsigned ce = c0 + lane;
       const bool vc = ce < NC;
@@ -2317,12 +2318,19 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
           nt = (unsigned)(pkc >> 60);
         }
       }
-      unsigned run_tot;
-      bool last;
-      const unsigned ex = seg_excl(nt, ui, &run_tot, &last);
-      const long long tb = vc ? TR[ui] : 0;
+      // The triangles of consecutive units are consecutive in conn, so a
+      // cell's first triangle is the task's first triangle plus the
+      // triangles of every cut cell before it in the task (in unit, then
+      // cell order): one warp scan per batch and a running carry.
+      unsigned incl = nt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const unsigned batch_tris = __shfl_sync(0xffffffffu, incl, 31);
       if (nt) {
-        const long long tpos = tb + ex;
+        const long long tpos = tcarry + (long long)(incl - nt);
         if (tpos < 0 || tpos + nt > A.conn_cap) {
           record_overflow(W.info);
         } else {
@@ -2338,9 +2346,7 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
           }
         }
       }
-      __syncwarp();
-      if (vc && last) TR[ui] = tb + run_tot;
-      __syncwarp();
+      tcarry += batch_tris;
     }
     __syncwarp();
   }
