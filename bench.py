@@ -68,8 +68,11 @@ def parse_args():
     ap.add_argument("--size", type=int, nargs=3, default=None,
                     help="override the volume's node counts (nx ny nz)")
     ap.add_argument("--e2e-steps", type=int, default=3)
-    ap.add_argument("--cpu-steps", type=int, default=5,
-                    help="timed steps of each CPU leg of cpu_baseline (after 2 untimed)")
+    ap.add_argument("--cpu-steps", type=int, default=8,
+                    help="timed steps of the reference leg of cpu_baseline (after 3 untimed)")
+    ap.add_argument("--ref-backend", choices=["cpu", "cuda"], default="cpu",
+                    help="--impl reference: the reference's tack.cpu (default) or its "
+                         "tack.cuda backend (NVRTC kernels; the whole volume, one GPU)")
     ap.add_argument("--install-reference", metavar="CHECKOUT", default=None,
                     help="copy the reference's Python sources from a berkgeveci/tack "
                          "checkout into baseline/_ref and exit")
@@ -382,12 +385,14 @@ def host_cores():
 def cpu_legs(sample, steps, warmup, port_steps=3):
     """Both CPU legs on the sample: the reference's tack.cpu (kind
     "reference"; the port alone, kind "port", when the reference cannot be
-    imported here) and the C port beside it.  Returns the cpu_baseline dict."""
+    imported here) and the C port beside it.  Each leg's value is the cells
+    of the sample (times the isovalues) over the median step time.  Returns
+    the cpu_baseline dict."""
     cores = host_cores()
     legs = {}
     try:
         t, threads = time_reference_cpu(sample, steps, warmup)
-        legs["reference"] = {"value": sample.cells * len(sample.isos) * len(t) / sum(t) / 1e9,
+        legs["reference"] = {"value": sample.cells * len(sample.isos) / statistics.median(t) / 1e9,
                              "cores": threads, "kind": "reference",
                              "seconds_per_step": statistics.median(t), "steps": len(t),
                              "what": "the reference's flying_edges on tack.cpu (llvmlite JIT), "
@@ -396,7 +401,7 @@ def cpu_legs(sample, steps, warmup, port_steps=3):
     except Exception as e:  # the reference could not be imported or run here
         legs["reference_error"] = f"{type(e).__name__}: {e}"
     t, nthreads = time_port_cpu(sample, port_steps, 1)
-    legs["port"] = {"value": sample.cells * len(sample.isos) * len(t) / sum(t) / 1e9,
+    legs["port"] = {"value": sample.cells * len(sample.isos) / statistics.median(t) / 1e9,
                     "cores": nthreads, "kind": "port", "seconds_per_step": statistics.median(t),
                     "steps": len(t),
                     "what": "the C restatement of the reference's kernels and host "
@@ -408,24 +413,87 @@ def cpu_legs(sample, steps, warmup, port_steps=3):
     return out
 
 
+def run_reference_cuda(args, local):
+    """The reference's flying_edges on its own CUDA backend (tack.cuda: NVRTC
+    kernels, one thread per row, host prefix sums between the passes) over
+    the whole volume on this GPU; each call as the reference makes it (its
+    zero mask filled on the host and copied in, the row arrays copied out and
+    summed on the host, the result copied back to numpy)."""
+    import torch
+    from tack_b200 import workloads
+    cfg = workloads.CONFIGS[args.config]
+    shape = tuple(args.size) if args.size else cfg["shape"]
+    nx, ny, nz = shape
+    vol = workloads.generate(args.config, shape, device=torch.device("cuda", local))
+    host = vol.cpu().numpy()
+    del vol
+    torch.cuda.synchronize()
+    paths = [os.path.join(REF_DIR, pkg, sub) for pkg, sub in REF_TREES]
+    for p in reversed(paths):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import tack as ref_tack
+    ref_tack.init(ref_tack.cuda)
+    from tack.algorithms.flying_edges import UniformGrid, flying_edges
+    f = ref_tack.field(dtype=ref_tack.f32, shape=(host.size,))
+    f.from_numpy(host)
+    g = UniformGrid(nx - 1, ny - 1, nz - 1, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
+    cells = (nx - 1) * (ny - 1) * (nz - 1)
+
+    def call():
+        t0 = time.perf_counter()
+        out = None
+        for iso in cfg["isovalues"]:
+            out = flying_edges(f, g, iso)
+        return time.perf_counter() - t0, out
+
+    for _ in range(max(1, args.warmup)):
+        call()
+    times = []
+    out = None
+    for _ in range(args.steps):
+        t, out = call()
+        times.append(t)
+    t = statistics.median(times)
+    value = cells / t / 1e9
+    line = {
+        "impl": "reference", "backend": "tack.cuda", "metric": METRIC, "value": value,
+        "unit": "Gcells/s", "n_gpus": 1, "steps": args.steps, "warmup": max(1, args.warmup),
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args.config, shape, cfg["isovalues"]),
+                   "volume_nodes": list(shape), "isovalues": cfg["isovalues"]},
+        "outputs": {"points": int(out["total_points"]) if out else 0,
+                    "triangles": int(out["total_tris"]) if out else 0},
+        "e2e": {"value": value, "unit": "Gcells/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": ("the reference's own GPU path: flying_edges on tack.cuda from baseline/_ref, "
+                 "the volume resident in a tack field, median wall time of whole calls"),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args):
     rank, world, local = dist_env()
     if rank != 0:
         return 0
+    if args.ref_backend == "cuda":
+        return run_reference_cuda(args, local)
     import torch
     from tack_b200 import workloads
     cfg = workloads.CONFIGS[args.config]
     shape = tuple(args.size) if args.size else cfg["shape"]
     device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
     sample = CpuSample(args.config, shape, cfg["isovalues"], device)
-    # JIT compilation takes the first calls: at least two untimed steps.
-    base = cpu_legs(sample, args.steps, max(2, args.warmup))
+    # JIT compilation takes the first calls: at least three untimed steps.
+    base = cpu_legs(sample, args.steps, max(3, args.warmup))
     head = base.get("reference") or base["port"]
     value = head["value"]
     ms = head["seconds_per_step"] * 1e3
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "Gcells/s",
-        "n_gpus": world, "steps": args.steps, "warmup": max(2, args.warmup),
+        "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
         "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload_name(args.config, shape, cfg["isovalues"]),
@@ -639,7 +707,7 @@ def main():
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         sample = CpuSample(args.config, shape, isos, dev, volume=vol)
-        cpu = cpu_legs(sample, args.cpu_steps, 2)
+        cpu = cpu_legs(sample, args.cpu_steps, 3)
 
     if world > 1:
         dist.barrier()

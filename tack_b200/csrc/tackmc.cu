@@ -488,7 +488,8 @@ struct FeIsoWs {
   long long* agg;       // [ntiles][4]
   long long* incl;      // [ntiles][4]
   long long* info;      // [16]: 0-3 own totals, 4-7 all-row totals, 8 active rows,
-                        //       9 tile counter, 10 error, 11 units, 12 own units
+                        //       9 tile counter, 10 error, 11 units, 12 own units,
+                        //       13 next emit task, 14 emit warps done
 };
 
 struct FeWsAll {
@@ -1055,12 +1056,23 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
       const int own = owner_lane(pre, ve ? e : NC - 1);
       const uint32_t ocand = __shfl_sync(0xffffffffu, cand, own);
       const unsigned opre = __shfl_sync(0xffffffffu, pre, own);
+      // The owner row's geometry from the owner lane (no division here).
+      RowQuad oq;
+      oq.fa = __shfl_sync(0xffffffffu, q.fa, own);
+      oq.j = __shfl_sync(0xffffffffu, q.j, own);
+      oq.k = __shfl_sync(0xffffffffu, q.k, own);
+      const unsigned oflags = __shfl_sync(0xffffffffu, (q.hasY ? 1u : 0u) | (q.hasZ ? 2u : 0u), own);
       uint32_t c = 0u;
       int w = 0;
       if (ve) {
         const int wb = nth_set_bit(ocand, (int)(e - opre));
         w = 32 * g + wb;
-        const RowQuad oq = row_quad(d, rbase + own);
+        oq.hasY = (oflags & 1u) != 0;
+        oq.hasZ = (oflags & 2u) != 0;
+        oq.hasC = oflags == 3u;
+        oq.fb = oq.hasY ? oq.fa + W : oq.fa;
+        oq.fc = oq.hasZ ? oq.fa + d.M * W : oq.fa;
+        oq.fd = oq.hasC ? oq.fc + W : oq.fb;
         c = count_word(load_word_quad(Wk.bits, oq, w, W), oq, w, Li, d, mask_b, s_ntri);
       }
       if (c != 0u) {
@@ -1420,12 +1432,12 @@ __device__ __forceinline__ void record_overflow(long long* info) {
 }
 
 // Device-planned bases whose global point total does not fit int32 ids are
-// negative (k_fe_plan_body).  The emit then writes nothing: thread 0 of each
-// block records TKMC_ERR_OVERFLOW (unless an earlier error is recorded) and
-// the whole block returns.  Host-given bases are never negative.
+// negative (k_fe_plan_body).  The emit then writes nothing: lane 0 of each
+// warp records TKMC_ERR_OVERFLOW (unless an earlier error is recorded) and
+// the caller skips its work.  Host-given bases are never negative.
 __device__ __forceinline__ bool ids_overflow(long long id_base, long long* info) {
   if (id_base >= 0) return false;
-  if (threadIdx.x == 0)
+  if ((threadIdx.x & 31) == 0)
     atomicCAS((unsigned long long*)(info + 10), 0ull, (unsigned long long)TKMC_ERR_OVERFLOW);
   return true;
 }
@@ -2141,15 +2153,19 @@ __global__ void __launch_bounds__(kThreads, 4)
 k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
   __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_case[tid] = c_case_groups[tid];  // kThreads == 256
+  __syncthreads();
+  // blockIdx.y = isovalue; the launch sizes each isovalue's grid row to one
+  // wave of resident blocks, whose warps take that isovalue's tasks.
   const int isoi = blockIdx.y;
+  const int wq = (int)(((int64_t)blockIdx.x * blockDim.x + tid) >> 5);
+  const int nwq = (int)(((int64_t)gridDim.x * blockDim.x) >> 5);
   const FeIsoWs W = iso_ws(ws, isoi);
   const float* __restrict__ vol = block_vol(ws, A.v);
   const int32_t* __restrict__ msk = block_mask(ws, A.mask);
   const float* gm = block_geom(ws, A.geom);
   const int bq = (int)blockIdx.z * (int)gridDim.y + isoi;  // bases of this block and isovalue
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  s_case[tid] = c_case_groups[tid];  // kThreads == 256
-  __syncthreads();
   const long long n_own = *((volatile long long*)(W.info + 12));
   uint32_t* U = s_rec[warp];
   const int Wd = d.W, Li = (int)d.L;
@@ -2163,15 +2179,25 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   const long long shX = base_out(A, bq, 0) - idX, shY = base_out(A, bq, 1) - idY,
                   shZ = base_out(A, bq, 2) - idZ;
   const long long outT = base_tri(A, bq);
-  if (ids_overflow(idX, W.info)) return;
-  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  // Units per warp task: 32, or 16 when the units make at most one task of
-  // 32 per warp -- then the longest task, not the number of tasks, sets the
-  // kernel's time, and halving the units per task shortens it (the small
-  // slabs of 8 GPUs).
-  const int G = n_own > 32 * nwarps ? 32 : 16;
-  for (int64_t grp = ((int64_t)blockIdx.x * blockDim.x + tid) >> 5; grp * G < n_own;
-       grp += nwarps) {
+  // Units per warp task: 32 when the units make at least two such tasks per
+  // warp, else 16 -- with few tasks the longest one, not their number, sets
+  // the kernel's time (the small slabs of 8 GPUs).
+  const int G = n_own > 64 * (long long)nwq ? 32 : 16;
+  // A warp's first task is its own index; every later one comes from a
+  // counter in the workspace (info[13], tasks taken past the first nwq): a
+  // warp that finishes early takes the next task, so the load balances, and
+  // the warps in flight work on neighbouring units (the volume rows they
+  // read are still in L2).  The index of a warp's next task is fetched while
+  // the current one runs.  The last warp of the launch to finish (counted in
+  // info[14]) sets both counters back to zero for the next launch; the count
+  // pass zeroes them too.
+  unsigned long long* next_task = reinterpret_cast<unsigned long long*>(W.info + 13);
+  unsigned long long* done_warps = reinterpret_cast<unsigned long long*>(W.info + 14);
+  long long grp = wq;
+  const bool overflow = ids_overflow(idX, W.info);
+  while (!overflow && grp * G < n_own) {
+    long long nxt = 0;
+    if (lane == 0) nxt = (long long)nwq + (long long)atomicAdd(next_task, 1ull);
     // ---- lane = unit ----
     const int64_t u = lane < G ? grp * G + lane : n_own;
     unsigned np = 0, nc = 0;
@@ -2349,6 +2375,15 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
       tcarry += batch_tris;
     }
     __syncwarp();
+    grp = __shfl_sync(0xffffffffu, nxt, 0);
+  }
+  if (lane == 0) {
+    __threadfence();  // this warp's last task fetch is ordered before its count
+    if (atomicAdd(done_warps, 1ull) == (unsigned long long)nwq - 1) {
+      __threadfence();
+      atomicExch(next_task, 0ull);
+      atomicExch(done_warps, 0ull);
+    }
   }
 }
 
@@ -3548,8 +3583,8 @@ static int fe_emit_impl(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
   if (f.d.AW <= kMaxAW) {
     const size_t smem = sizeof(EmitSmem);
     if ((rc = ensure_smem(k_fe_emit_words, smem, g_smem_emit_words))) return rc;
-    if (f.unit_cap > 0) {  // word-aligned rows: the unit list
-      k_fe_emit_units<<<dim3((unsigned)(sm_count() * 8), (unsigned)niso), kThreads, 0, st>>>(
+    if (f.unit_cap > 0) {  // word-aligned rows: the unit list; one wave of blocks per isovalue
+      k_fe_emit_units<<<dim3((unsigned)(sm_count() * 4), (unsigned)niso), kThreads, 0, st>>>(
           f.d, v, A);
       TK_LAUNCHED();
       return TKMC_OK;
