@@ -1117,6 +1117,123 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   }
 }
 
+// K2a with the candidate words of the whole block shared by its 256 threads
+// (word-aligned rows, grids of few blocks: the small slabs of several GPUs).
+// The rows' candidates are listed block-wide (a block prefix of the per-row
+// counts in shared memory, with each row's geometry), then thread = candidate
+// over the whole list, so the block takes as long as its average warp rather
+// than its busiest one: one warp's 32 rows can hold most of the block's
+// surface.  Same outputs as k_fe_count_words.
+__global__ void __launch_bounds__(kThreads)
+k_fe_count_words_bal(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
+  __shared__ int s_ntri[256];
+  __shared__ unsigned s_cnt[4][kThreads];
+  __shared__ unsigned s_nu[kThreads];
+  __shared__ uint32_t s_act[kThreads];
+  __shared__ uint32_t s_cand[kThreads];
+  __shared__ unsigned s_pre[kThreads];
+  __shared__ unsigned s_wsum[kThreads / 32];
+  __shared__ long long s_fa[kThreads];
+  __shared__ uint32_t s_j[kThreads], s_k[kThreads], s_fl[kThreads];
+  const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
+  const int32_t* __restrict__ mask_b = block_mask(ws, mask);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256
+#pragma unroll
+  for (int t = 0; t < 4; ++t) s_cnt[t][tid] = 0;
+  s_nu[tid] = 0;
+  const int64_t rbase = (int64_t)blockIdx.x * kThreads;  // the block's first row
+  const int64_t r = rbase + tid;
+  const bool valid = r < d.R;
+  const int W = d.W, Li = (int)d.L;
+  RowQuad q{};
+  if (valid) q = row_quad(d, r);
+  s_fa[tid] = q.fa;
+  s_j[tid] = q.j;
+  s_k[tid] = q.k;
+  s_fl[tid] = (q.hasY ? 1u : 0u) | (q.hasZ ? 2u : 0u);
+  for (int g = 0; g < d.AW; ++g) {
+    const uint32_t cand = valid ? candidates(Wk.sums, q, W, g) : 0u;
+    const unsigned nc = __popc(cand);
+    unsigned pre = nc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, pre, o);
+      if (lane >= o) pre += y;
+    }
+    if (lane == 31) s_wsum[warp] = pre;
+    s_cand[tid] = cand;
+    s_act[tid] = 0u;
+    __syncthreads();
+    unsigned before = 0, NC = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < kThreads / 32; ++w2) {
+      const unsigned x = s_wsum[w2];
+      before += w2 < warp ? x : 0u;
+      NC += x;
+    }
+    s_pre[tid] = before + pre - nc;  // block-exclusive prefix of the row's candidates
+    __syncthreads();
+    for (unsigned e = tid; e < NC; e += kThreads) {
+      // The row holding candidate e: the last row whose prefix is <= e (rows
+      // without candidates share the prefix of the next row that has some).
+      int own = 0;
+#pragma unroll
+      for (int step = kThreads / 2; step >= 1; step >>= 1)
+        if (s_pre[own + step] <= e) own += step;
+      const int wb = nth_set_bit(s_cand[own], (int)(e - s_pre[own]));
+      const int w = 32 * g + wb;
+      RowQuad oq;
+      oq.fa = s_fa[own];
+      oq.j = s_j[own];
+      oq.k = s_k[own];
+      const uint32_t fl = s_fl[own];
+      oq.hasY = (fl & 1u) != 0;
+      oq.hasZ = (fl & 2u) != 0;
+      oq.hasC = fl == 3u;
+      oq.fb = oq.hasY ? oq.fa + W : oq.fa;
+      oq.fc = oq.hasZ ? oq.fa + d.M * W : oq.fa;
+      oq.fd = oq.hasC ? oq.fc + W : oq.fb;
+      const uint32_t c = count_word(load_word_quad(Wk.bits, oq, w, W), oq, w, Li, d, mask_b, s_ntri);
+      if (c != 0u) {
+        atomicAdd(&s_cnt[0][own], c & 63u);
+        atomicAdd(&s_cnt[1][own], (c >> 6) & 63u);
+        atomicAdd(&s_cnt[2][own], (c >> 12) & 63u);
+        atomicAdd(&s_cnt[3][own], c >> 18);
+        atomicOr(&s_act[own], 1u << (w & 31));
+        Wk.wcnt[(rbase + own) * W + w] = c;
+      }
+    }
+    __syncthreads();
+    if (valid) {
+      Wk.wact[r * d.AW + g] = s_act[tid];
+      s_nu[tid] += __popc(s_act[tid]);
+    }
+    __syncthreads();
+  }
+  long long own5[5] = {0, 0, 0, 0, 0};
+  if (valid) {
+    reinterpret_cast<int4*>(Wk.cnt)[r] =
+        make_int4((int)s_cnt[0][tid], (int)s_cnt[1][tid], (int)s_cnt[2][tid], (int)s_cnt[3][tid]);
+    Wk.ucnt[r] = s_nu[tid];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) own5[t] = s_cnt[t][tid];
+    own5[4] = s_nu[tid];
+  }
+#pragma unroll
+  for (int t = 0; t < 5; ++t) {
+    long long x = own5[t];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == t && x != 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(Wk.agg + blockIdx.x * 5 + t),
+                (unsigned long long)x);
+      atomicAdd(reinterpret_cast<unsigned long long*>(Wk.super + (blockIdx.x / kSuperTiles) * 5 + t),
+                (unsigned long long)x);
+    }
+  }
+}
+
 // K2b (word-aligned rows): the first unit of each row, the units and the
 // totals (rows_only: the row offsets instead, for tkmc_fe_row_offsets).  The
 // tile's prefix is the sum of the super-tile totals before its super-tile
@@ -3439,7 +3556,13 @@ static int fe_scan_impl(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int
   const int64_t skip = g_skip_tile.exchange(-1);
   if (aligned) {  // no waits between blocks here: the skip hook does not apply
     const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
-    k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
+    // Grids of at most about two waves of blocks (the small slabs of
+    // several GPUs) end when their busiest block does: share each block's
+    // candidates among all its warps there.
+    if (f.d.ntiles * niso <= (int64_t)sm_count() * 8)
+      k_fe_count_words_bal<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
+    else
+      k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
     TK_LAUNCHED();
     if (parts & 2) {
       k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, f.unit_cap, 0);
