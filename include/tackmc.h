@@ -208,7 +208,8 @@ int tkmc_fe_emit_dev(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
 
 /* Copy the own totals {X, Y, Z, T} per isovalue (niso*4 int64) that the
  * last count left in the workspace to dst (device memory or page-locked
- * host memory).  Asynchronous. */
+ * host memory; a one-warp kernel stores them when the device can address
+ * dst, a copy otherwise).  Asynchronous. */
 int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso,
                         const void* workspace, size_t workspace_bytes,
                         int64_t* dst, void* stream);

@@ -2808,6 +2808,14 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
 }
 
 
+// This workspace's own totals {X, Y, Z, T} of each isovalue (info words
+// 16q + 0..3) to dst[4q + 0..3] (device memory or mapped host memory).
+__global__ void k_fe_copy_totals(const long long* __restrict__ info, int niso,
+                                 long long* __restrict__ dst) {
+  const int i = threadIdx.x;
+  if (i < 4 * niso) dst[i] = __ldcg(info + 16 * (i >> 2) + (i & 3));
+}
+
 // Forget capacity errors recorded by an emit (device timeouts stay).
 __global__ void k_fe_clear_capacity_error(FeWsAll ws, int niso) {
   const int q = threadIdx.x;
@@ -3751,10 +3759,26 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso, const void
   int rc = check_ws(const_cast<void*>(ws), ws_bytes, f.total);
   if (rc) return rc;
   if (!dst) return set_err(TKMC_ERR_INVALID_ARG, "dst is NULL");
-  TK_CUDA(cudaMemcpy2DAsync(dst, 4 * sizeof(long long),
-                            static_cast<const char*>(ws) + f.off_info, 16 * sizeof(long long),
-                            4 * sizeof(long long), (size_t)niso, cudaMemcpyDefault,
-                            static_cast<cudaStream_t>(stream)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long* info =
+      reinterpret_cast<const long long*>(static_cast<const char*>(ws) + f.off_info);
+  // Device memory, or page-locked host memory the device can address: one
+  // tiny kernel stores the totals (a copy-engine transfer at the end of a
+  // graph-launched step costs several microseconds more).  Other host
+  // memory: a copy.
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, dst) == cudaSuccess &&
+      (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged ||
+       (at.type == cudaMemoryTypeHost && at.devicePointer != nullptr))) {
+    long long* d = static_cast<long long*>(at.type == cudaMemoryTypeHost ? at.devicePointer
+                                                                         : static_cast<void*>(dst));
+    k_fe_copy_totals<<<1, 32, 0, st>>>(info, niso, d);
+    TK_LAUNCHED();
+    return TKMC_OK;
+  }
+  cudaGetLastError();  // a pointer the runtime does not know is not an error here
+  TK_CUDA(cudaMemcpy2DAsync(dst, 4 * sizeof(long long), info, 16 * sizeof(long long),
+                            4 * sizeof(long long), (size_t)niso, cudaMemcpyDefault, st));
   return TKMC_OK;
 }
 
