@@ -3762,13 +3762,14 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso, const void
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const long long* info =
       reinterpret_cast<const long long*>(static_cast<const char*>(ws) + f.off_info);
-  // Device memory, or page-locked host memory the device can address: one
-  // tiny kernel stores the totals (a copy-engine transfer at the end of a
-  // graph-launched step costs several microseconds more).  Other host
-  // memory: a copy.
+  // This device's memory, or page-locked host memory the device can
+  // address: one tiny kernel stores the totals (a copy-engine transfer at
+  // the end of a graph-launched step costs several microseconds more).
+  // Anything else (pageable host memory, another GPU's memory): a copy.
   cudaPointerAttributes at{};
-  if (cudaPointerGetAttributes(&at, dst) == cudaSuccess &&
-      (at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged ||
+  int dev = -1;
+  if (cudaPointerGetAttributes(&at, dst) == cudaSuccess && cudaGetDevice(&dev) == cudaSuccess &&
+      ((at.type == cudaMemoryTypeDevice && at.device == dev) ||
        (at.type == cudaMemoryTypeHost && at.devicePointer != nullptr))) {
     long long* d = static_cast<long long*>(at.type == cudaMemoryTypeHost ? at.devicePointer
                                                                          : static_cast<void*>(dst));

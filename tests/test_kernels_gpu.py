@@ -167,3 +167,34 @@ def test_soup_matches_oracle(tack, oracle, shape):
     keep = np.repeat(mask == 0, 3 * ntri)  # the soup without the masked cells' triangles
     assert rm["total_tris"] == int(ntri[mask == 0].sum())
     _nan_aware_equal(rm["x"], x[keep])
+
+
+def test_copy_counts_to_device_pinned_and_pageable_memory(tack):
+    """tkmc_fe_copy_counts writes the same totals whether the destination is
+    this GPU's memory or page-locked host memory (a kernel store) or pageable
+    host memory (a copy), and they equal tkmc_fe_read_counts'."""
+    import ctypes
+    from tack_b200 import _lib, workloads
+    from fe_helpers import f32arr, stream
+    lib = _lib.load()
+    shape = (128, 96, 80)
+    nx, ny, nz = shape[0] - 1, shape[1] - 1, shape[2] - 1
+    vol = workloads.generate("blobs", shape)
+    isos = [0.5, 0.9, 0.2]
+    nb = lib.tkmc_fe_workspace_bytes(nx, ny, nz, len(isos))
+    ws = torch.empty(nb, dtype=torch.uint8, device="cuda")
+    want = np.zeros(4 * len(isos), np.int64)
+    _lib.check(lib.tkmc_fe_count(vol.data_ptr(), nx, ny, nz, 0, f32arr(isos), len(isos), None,
+                                 ws.data_ptr(), nb, want.ctypes.data, stream()), "count")
+    assert want.sum() > 0
+    dev = torch.full((4 * len(isos),), -1, dtype=torch.int64, device="cuda")
+    pinned = torch.full((4 * len(isos),), -1, dtype=torch.int64, pin_memory=True)
+    pageable = np.full(4 * len(isos), -1, np.int64)
+    for ptr in (dev.data_ptr(), pinned.data_ptr(), pageable.ctypes.data):
+        _lib.check(lib.tkmc_fe_copy_counts(nx, ny, nz, len(isos), ws.data_ptr(), nb, ptr,
+                                           stream()), "copy_counts")
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(dev.cpu().numpy(), want)
+    np.testing.assert_array_equal(pinned.numpy(), want)
+    np.testing.assert_array_equal(pageable, want)
+    del ctypes
