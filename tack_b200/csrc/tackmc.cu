@@ -153,6 +153,16 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization (launch_pdl) may start while the kernel before it in the
+// stream is still running; griddep_wait() returns once that kernel has
+// completed and its writes are visible, so it comes before the first read of
+// anything the predecessor writes (it returns at once after a normal
+// launch).  griddep_launch() lets the next such kernel launch as soon as
+// every block of this grid has issued it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
 // p moved by off bytes.
 template <typename T>
 __device__ __forceinline__ T* shift_ptr(T* p, int64_t off) {
@@ -358,6 +368,7 @@ k_fe_threshold_words(const float* __restrict__ v, int64_t nfull, IsoParams iso,
                      uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
                      uint2* __restrict__ sums, int64_t sums_stride, int64_t nchunks,
                      int64_t ws_stride, const float* const* vols) {
+  griddep_launch();
   // A batch of same-shape blocks: blockIdx.z picks the block.
   if (vols) v = vols[blockIdx.z];
   bits = shift_ptr(bits, (int64_t)blockIdx.z * ws_stride);
@@ -405,6 +416,7 @@ k_fe_threshold_scalar(const float* __restrict__ v, int64_t n, IsoParams iso, int
                       uint32_t* __restrict__ bits, int64_t bits_stride, int64_t nwords,
                       uint2* __restrict__ sums, int64_t sums_stride, int64_t first_chunk,
                       int64_t ws_stride, const float* const* vols) {
+  griddep_launch();
   // A batch of same-shape blocks: blockIdx.z picks the block.
   if (vols) v = vols[blockIdx.z];
   bits = shift_ptr(bits, (int64_t)blockIdx.z * ws_stride);
@@ -1026,10 +1038,12 @@ k_fe_count_words(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
   const int32_t* __restrict__ mask_b = block_mask(ws, mask);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_launch();
   s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256
 #pragma unroll
   for (int t = 0; t < 4; ++t) s_cnt[t][tid] = 0;
   s_nu[tid] = 0;
+  griddep_wait();  // the bitmask and summaries of the threshold pass
   __syncthreads();
   const int64_t rbase = (int64_t)blockIdx.x * kThreads + warp * 32;  // the warp's first row
   const int64_t r = rbase + lane;
@@ -1138,10 +1152,12 @@ k_fe_count_words_bal(FeDims d, FeWsAll ws, const int32_t* __restrict__ mask) {
   const FeIsoWs Wk = iso_ws(ws, blockIdx.y);
   const int32_t* __restrict__ mask_b = block_mask(ws, mask);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_launch();
   s_ntri[tid] = (int)(c_case_tris[tid] >> 60);  // kThreads == 256
 #pragma unroll
   for (int t = 0; t < 4; ++t) s_cnt[t][tid] = 0;
   s_nu[tid] = 0;
+  griddep_wait();  // the bitmask and summaries of the threshold pass
   const int64_t rbase = (int64_t)blockIdx.x * kThreads;  // the block's first row
   const int64_t r = rbase + tid;
   const bool valid = r < d.R;
@@ -1254,6 +1270,8 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, int64_t unit_cap, int rows_only) {
   const int64_t rbase = tile * kThreads + warp * 32;  // the warp's first row
   const int64_t r = rbase + lane;
   const bool valid = r < d.R;
+  griddep_launch();
+  griddep_wait();  // the count pass's row counts and tile totals
   if (warp < 5) {  // warp k sums value k of the tile's prefix and of the grand total
     const int k = warp;
     const int64_t nsup = (d.ntiles + kSuperTiles - 1) / kSuperTiles, sup = tile / kSuperTiles;
@@ -2271,7 +2289,9 @@ k_fe_emit_units(FeDims d, FeWsAll ws, FeEmitArgs A) {
   __shared__ uint64_t s_case[256];
   __shared__ uint32_t s_rec[kThreads / 32][32 * kUS];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  griddep_launch();
   s_case[tid] = c_case_groups[tid];  // kThreads == 256
+  griddep_wait();  // units, bit words and bases of the passes before
   __syncthreads();
   // blockIdx.y = isovalue; the launch sizes each isovalue's grid row to one
   // wave of resident blocks, whose warps take that isovalue's tasks.
@@ -2671,6 +2691,8 @@ __device__ void k_fe_plan_body(const long long* c, int world, int rank, int niso
 
 __global__ void k_fe_plan(const long long* __restrict__ c, int world, int rank, int niso,
                           int shared_output, long long* __restrict__ bases) {
+  griddep_launch();
+  griddep_wait();
   if (threadIdx.x == 0 && blockIdx.x == 0) k_fe_plan_body(c, world, rank, niso, shared_output, bases);
 }
 
@@ -2808,11 +2830,26 @@ __global__ void k_fe_exchange_plan(ExchangePeers peers, unsigned long long* epoc
 }
 
 
+// Zero the per-call state of a workspace (n8 8-byte words) before a count
+// pass.  Launched right behind the threshold pass, which writes none of it,
+// so it runs beside that pass's last blocks; it completes only after the
+// threshold pass has (griddep_wait at the end), so a kernel that waits on it
+// also sees the bitmask.
+__global__ void k_fe_reset(unsigned long long* __restrict__ p, int64_t n8) {
+  griddep_launch();
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8;
+       i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = 0ull;
+  griddep_wait();
+}
+
 // This workspace's own totals {X, Y, Z, T} of each isovalue (info words
 // 16q + 0..3) to dst[4q + 0..3] (device memory or mapped host memory).
 __global__ void k_fe_copy_totals(const long long* __restrict__ info, int niso,
                                  long long* __restrict__ dst) {
   const int i = threadIdx.x;
+  griddep_launch();
+  griddep_wait();
   if (i < 4 * niso) dst[i] = __ldcg(info + 16 * (i >> 2) + (i & 3));
 }
 
@@ -3246,6 +3283,27 @@ int ensure_smem(F* kernel, size_t bytes, std::atomic<size_t>* per_device) {
 std::atomic<size_t> g_smem_count[64];
 std::atomic<size_t> g_smem_emit_words[64];
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the kernel before it in the stream is still running (it waits for it in
+// griddep_wait before reading its results), so its launch and prologue
+// overlap the predecessor's last blocks.  Inside stream capture this becomes
+// a programmatic edge of the graph.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 int check_ws(void* ws, size_t have, size_t need) {
   if (need && !ws) return set_err(TKMC_ERR_INVALID_ARG, "workspace is NULL");
   if (have < need)
@@ -3554,13 +3612,19 @@ static int fe_scan_impl(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int
   const bool aligned = (f.d.L & 31) == 0;
   if (!(parts & 1)) {
     if (aligned) {
-      k_fe_offsets_units<<<dim3((unsigned)f.d.ntiles, (unsigned)niso), kThreads, 0, st>>>(
-          f.d, v, f.unit_cap, 0);
+      TK_CUDA(launch_pdl(k_fe_offsets_units, dim3((unsigned)f.d.ntiles, (unsigned)niso),
+                         dim3(kThreads), 0, st, f.d, v, f.unit_cap, 0));
       TK_LAUNCHED();
     }
     return TKMC_OK;
   }
-  TK_CUDA(cudaMemsetAsync(static_cast<char*>(ws) + f.off_info, 0, f.reset_bytes - f.off_info, st));
+  {  // zero the per-call state (info, tile flags and totals)
+    const int64_t n8 = (int64_t)(f.reset_bytes - f.off_info) / 8;
+    TK_CUDA(launch_pdl(k_fe_reset, dim3((unsigned)grid_for(n8, kThreads, 2)), dim3(kThreads), 0,
+                       st, reinterpret_cast<unsigned long long*>(static_cast<char*>(ws) + f.off_info),
+                       n8));
+    TK_LAUNCHED();
+  }
   const int64_t skip = g_skip_tile.exchange(-1);
   if (aligned) {  // no waits between blocks here: the skip hook does not apply
     const dim3 tiles((unsigned)f.d.ntiles, (unsigned)niso);
@@ -3568,12 +3632,12 @@ static int fe_scan_impl(int64_t nx, int64_t ny, int64_t nz, int ghost_plane, int
     // several GPUs) end when their busiest block does: share each block's
     // candidates among all its warps there.
     if (f.d.ntiles * niso <= (int64_t)sm_count() * 8)
-      k_fe_count_words_bal<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
+      TK_CUDA(launch_pdl(k_fe_count_words_bal, tiles, dim3(kThreads), 0, st, f.d, v, mask));
     else
-      k_fe_count_words<<<tiles, kThreads, 0, st>>>(f.d, v, mask);
+      TK_CUDA(launch_pdl(k_fe_count_words, tiles, dim3(kThreads), 0, st, f.d, v, mask));
     TK_LAUNCHED();
     if (parts & 2) {
-      k_fe_offsets_units<<<tiles, kThreads, 0, st>>>(f.d, v, f.unit_cap, 0);
+      TK_CUDA(launch_pdl(k_fe_offsets_units, tiles, dim3(kThreads), 0, st, f.d, v, f.unit_cap, 0));
       TK_LAUNCHED();
     }
     return TKMC_OK;
@@ -3715,8 +3779,8 @@ static int fe_emit_impl(const float* scalar, int64_t nx, int64_t ny, int64_t nz,
     const size_t smem = sizeof(EmitSmem);
     if ((rc = ensure_smem(k_fe_emit_words, smem, g_smem_emit_words))) return rc;
     if (f.unit_cap > 0) {  // word-aligned rows: the unit list; one wave of blocks per isovalue
-      k_fe_emit_units<<<dim3((unsigned)(sm_count() * 4), (unsigned)niso), kThreads, 0, st>>>(
-          f.d, v, A);
+      TK_CUDA(launch_pdl(k_fe_emit_units, dim3((unsigned)(sm_count() * 4), (unsigned)niso),
+                         dim3(kThreads), 0, st, f.d, v, A));
       TK_LAUNCHED();
       return TKMC_OK;
     }
@@ -3773,7 +3837,7 @@ int tkmc_fe_copy_counts(int64_t nx, int64_t ny, int64_t nz, int niso, const void
        (at.type == cudaMemoryTypeHost && at.devicePointer != nullptr))) {
     long long* d = static_cast<long long*>(at.type == cudaMemoryTypeHost ? at.devicePointer
                                                                          : static_cast<void*>(dst));
-    k_fe_copy_totals<<<1, 32, 0, st>>>(info, niso, d);
+    TK_CUDA(launch_pdl(k_fe_copy_totals, dim3(1), dim3(32), 0, st, info, niso, d));
     TK_LAUNCHED();
     return TKMC_OK;
   }
@@ -4082,9 +4146,9 @@ int tkmc_fe_plan(const int64_t* all_counts_dev, int world, int rank, int niso,
   if (!all_counts_dev || !bases_dev) return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_plan: NULL");
   if (world < 1 || rank < 0 || rank >= world || niso < 1 || niso > TKMC_MAX_ISO)
     return set_err(TKMC_ERR_INVALID_ARG, "tkmc_fe_plan: bad world/rank/niso");
-  k_fe_plan<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<const long long*>(all_counts_dev), world, rank, niso, shared_output,
-      reinterpret_cast<long long*>(bases_dev));
+  TK_CUDA(launch_pdl(k_fe_plan, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+                     reinterpret_cast<const long long*>(all_counts_dev), world, rank, niso,
+                     shared_output, reinterpret_cast<long long*>(bases_dev)));
   TK_LAUNCHED();
   return TKMC_OK;
 }
