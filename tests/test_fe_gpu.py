@@ -3,8 +3,8 @@
 Every golden fixture was produced by the reference (tack.cpu).  The GPU
 result must be identical: totals, per-row offsets (scan), connectivity, and
 point coordinates bit for bit (the kernels use the reference's f32
-operation order without contraction; the tolerance the north star allows,
-1e-5 relative, is not needed).
+operation order without contraction; the 1e-5 relative tolerance allowed
+for vertex positions is not needed).
 """
 
 import numpy as np
