@@ -1272,6 +1272,16 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, int64_t unit_cap, int rows_only) {
   const bool valid = r < d.R;
   griddep_launch();
   griddep_wait();  // the count pass's row counts and tile totals
+  // The row's counts (and, for rows of one activity word, that word) are
+  // loaded before the tile prefix, so both loads are in flight together.
+  int4 c = make_int4(0, 0, 0, 0);
+  unsigned nU = 0;
+  uint32_t wa0 = 0;
+  if (valid) {
+    c = __ldcg(reinterpret_cast<const int4*>(Wk.cnt) + r);
+    nU = __ldcg(Wk.ucnt + r);
+    if (d.AW == 1 && !rows_only) wa0 = __ldcg(Wk.wact + r);
+  }
   if (warp < 5) {  // warp k sums value k of the tile's prefix and of the grand total
     const int k = warp;
     const int64_t nsup = (d.ntiles + kSuperTiles - 1) / kSuperTiles, sup = tile / kSuperTiles;
@@ -1291,12 +1301,6 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, int64_t unit_cap, int rows_only) {
       s_pre[k] = pre;
       s_all[k] = all;
     }
-  }
-  int4 c = make_int4(0, 0, 0, 0);
-  unsigned nU = 0;
-  if (valid) {
-    c = __ldcg(reinterpret_cast<const int4*>(Wk.cnt) + r);
-    nU = __ldcg(Wk.ucnt + r);
   }
   const long long own[5] = {c.x, c.y, c.z, c.w, nU};
   long long inc[5];
@@ -1373,7 +1377,11 @@ k_fe_offsets_units(FeDims d, FeWsAll ws, int64_t unit_cap, int rows_only) {
     const int64_t orow = rbase + own_l;
     int w = 0;
     uint32_t cw = 0;
-    if (ve) {
+    const uint32_t om = __shfl_sync(0xffffffffu, wa0, own_l);
+    if (ve && d.AW == 1) {
+      w = nth_set_bit(om, (int)(e - opre));
+      cw = __ldcg(Wk.wcnt + orow * d.W + w);
+    } else if (ve) {
       int k = (int)(e - opre);  // k-th active word of the row
       for (int i = 0; i < d.AW; ++i) {
         const uint32_t m = __ldcg(Wk.wact + orow * d.AW + i);
