@@ -80,10 +80,15 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="totals exchange between ranks (N>1): NVLink peer stores or NCCL")
-    ap.add_argument("--balance-slabs", action="store_true",
-                    help="N>1: node-plane runs balanced by the surface of a first pass "
-                         "instead of equal runs")
-    return ap.parse_args()
+    ap.add_argument("--slabs", choices=["measured", "surface", "equal"], default="measured",
+                    help="N>1: node-plane runs per rank: equal runs moved toward equal "
+                         "measured device time per rank (default), runs balanced by the "
+                         "surface of a first pass, or equal runs")
+    ap.add_argument("--balance-slabs", action="store_true", help="the same as --slabs surface")
+    args = ap.parse_args()
+    if args.balance_slabs:
+        args.slabs = "surface"
+    return args
 
 
 def dist_env():
@@ -532,7 +537,8 @@ def main():
 
     import tack_b200 as tack
     from tack_b200 import _lib, workloads
-    from tack_b200.distributed import SlabEngine, SlabPlan, balanced_bounds, slab_bases
+    from tack_b200.distributed import (SlabEngine, SlabPlan, balanced_bounds,
+                                       rebalanced_bounds, slab_bases)
 
     rank, world, local = dist_env()
     if world != args.gpus:
@@ -546,77 +552,97 @@ def main():
     shape = tuple(args.size) if args.size else cfg["shape"]
     isos = cfg["isovalues"]
     nxn, nyn, nzn = shape
-    plan = SlabPlan(nzn, world, rank)
     grid = tack.UniformGrid(nxn - 1, nyn - 1, nzn - 1, 0.0, 0.0, 0.0, 1.0, 1.0, 1.0)
-    vol = workloads.generate(args.config, shape, plan.k0, plan.k1, device=dev)
-    torch.cuda.synchronize()
-    eng = SlabEngine(grid, plan, isos, exchange=args.exchange)
     lib = _lib.load()
     stream = torch.cuda.current_stream(dev)
     niso = len(isos)
     isoc = (ctypes_f32(isos))
-    local_nodes = vol.numel()
     cells = (nxn - 1) * (nyn - 1) * (nzn - 1)
+    counts_host = torch.zeros(niso * 4, dtype=torch.int64, pin_memory=True)
+    K = args.steps
+    KP = min(K, 50)
 
-    # Output buffers of this rank's exact size, from one host-planned run;
-    # the timed steps then run count -> plan -> emit with no host round trip
-    # (the totals reach the host asynchronously, as a caller would read them).
-    first = eng.run(vol)
-    own = first["counts"]
+    def setup(bounds):
+        """This rank's slab on `bounds` (None: equal runs): its volume, engine,
+        one host-planned run, and output buffers of its exact size; the timed
+        steps then run count -> plan -> emit with no host round trip (the
+        totals reach the host asynchronously, as a caller would read them)."""
+        plan = SlabPlan(nzn, world, rank, bounds=bounds)
+        vol = workloads.generate(args.config, shape, plan.k0, plan.k1, device=dev)
+        torch.cuda.synchronize()
+        eng = SlabEngine(grid, plan, isos, exchange=args.exchange)
+        first = eng.run(vol)
+        own = first["counts"]
+        own_p, own_t = int(own[:, :3].sum()), int(own[:, 3].sum())
+        pts_buf = torch.empty(max(own_p, 1) * 3, dtype=torch.float32, device=dev)
+        conn_buf = torch.empty(max(own_t, 1) * 3, dtype=torch.int32, device=dev)
+        return plan, vol, eng, first, pts_buf, conn_buf
+
+    def phases(eng, vol, pts_buf, conn_buf):
+        """Warm-up steps, then phase times: CUDA events between the phases of
+        KP ordinary (not graph) steps (ms: threshold, count, totals exchange /
+        plan, emit); the headline time is measured separately."""
+        for _ in range(args.warmup):
+            eng.run_device(vol, pts_buf, conn_buf, counts_host)
+        ev = {k: [torch.cuda.Event(enable_timing=True) for _ in range(KP)] for k in "abcde"}
+        for i in range(KP):
+            eng.run_device(vol, pts_buf, conn_buf, counts_host, [ev[k][i] for k in "abcde"])
+        torch.cuda.synchronize()
+
+        def mean(a, b):
+            return sum(ev[a][i].elapsed_time(ev[b][i]) for i in range(KP)) / KP
+        return mean("a", "b"), mean("b", "c"), mean("c", "d"), mean("d", "e")
+
     balanced = None
-    if world > 1 and args.balance_slabs:
+    plan, vol, eng, first, pts_buf, conn_buf = setup(None)
+    if world > 1 and args.slabs == "surface":
         # Slab bounds balanced by predicted device time: the surface of this
         # first pass (in a time series, the previous step's) gives each node
         # plane's triangles; a plane costs NODE_COST per node (the threshold
         # read) plus TRI_COST per triangle (count and emit).  Then the slabs
         # are set up again on the new bounds.
-        tris = eng.plane_triangles(own)
+        tris = eng.plane_triangles(first["counts"])
         allt = [None] * world
         dist.all_gather_object(allt, tris.tolist())
         plane_tris = np.concatenate([np.asarray(t, np.float64) for t in allt])
         work = NODE_COST * nxn * nyn + TRI_COST * plane_tris
         balanced = balanced_bounds(work, world)
         eng.close()
-        del eng, vol, first
-        plan = SlabPlan(nzn, world, rank, bounds=balanced)
-        vol = workloads.generate(args.config, shape, plan.k0, plan.k1, device=dev)
-        torch.cuda.synchronize()
-        eng = SlabEngine(grid, plan, isos, exchange=args.exchange)
-        local_nodes = vol.numel()
-        first = eng.run(vol)
-        own = first["counts"]
+        del eng, vol, first, pts_buf, conn_buf
+        plan, vol, eng, first, pts_buf, conn_buf = setup(balanced)
+    k1, k2, host, k3 = phases(eng, vol, pts_buf, conn_buf)
+    moves = []
+    if world > 1 and args.slabs == "measured":
+        # Bounds moved toward equal device time per rank, from every rank's
+        # measured threshold + count + emit time on the current bounds (the
+        # exchange wait left out), at most twice; every rank gets the same
+        # gathered times, so all take the same decision.
+        for _ in range(2):
+            t = torch.tensor([k1, k1 + k2 + k3, float(plan.p0), float(plan.p1)],
+                             dtype=torch.float64, device=dev)
+            allt = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(allt, t)
+            allt = np.stack([a.cpu().numpy() for a in allt])
+            cur = [int(x) for x in allt[:, 2]] + [int(allt[-1, 3])]
+            new = rebalanced_bounds(cur, allt[:, 0], allt[:, 1])
+            if max(abs(a - b) for a, b in zip(new, cur)) <= 1:
+                break
+            moves.append({"bounds": cur, "busy_ms": [round(float(x), 4) for x in allt[:, 1]]})
+            balanced = new
+            eng.close()
+            del eng, vol, first, pts_buf, conn_buf
+            plan, vol, eng, first, pts_buf, conn_buf = setup(balanced)
+            k1, k2, host, k3 = phases(eng, vol, pts_buf, conn_buf)
+    local_nodes = vol.numel()
+    own = first["counts"]
     own_p, own_t = int(own[:, :3].sum()), int(own[:, 3].sum())
-    pts_buf = torch.empty(max(own_p, 1) * 3, dtype=torch.float32, device=dev)
-    conn_buf = torch.empty(max(own_t, 1) * 3, dtype=torch.int32, device=dev)
-    counts_host = torch.zeros(niso * 4, dtype=torch.int64, pin_memory=True)
     bases = first["bases"]
-    ev = {}
-
-    def step(i=None):
-        marks = [ev[k][i] for k in "abcde"] if i is not None else None
-        eng.run_device(vol, pts_buf, conn_buf, counts_host, marks)
 
     def barrier():
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        step()
-    K = args.steps
-    # Phase times: CUDA events between the phases of ordinary (not graph)
-    # steps, after the warm-up; the headline time is measured below.
-    KP = min(K, 50)
-    for key in "abcde":
-        ev[key] = [torch.cuda.Event(enable_timing=True) for _ in range(KP)]
-    for i in range(KP):
-        step(i)
-    torch.cuda.synchronize()
-    k1 = sum(ev["a"][i].elapsed_time(ev["b"][i]) for i in range(KP)) / KP
-    k2 = sum(ev["b"][i].elapsed_time(ev["c"][i]) for i in range(KP)) / KP
-    k3 = sum(ev["d"][i].elapsed_time(ev["e"][i]) for i in range(KP)) / KP
-    host = sum(ev["c"][i].elapsed_time(ev["d"][i]) for i in range(KP)) / KP  # totals + plan
     # The whole step, the totals all-gather included, is one CUDA graph: one
     # host launch per step on every rank.
     launches0 = lib.tkmc_launch_count()
@@ -730,9 +756,10 @@ def main():
                 "volume_nodes": list(shape), "cells": cells, "isovalues": isos,
                 "parallelism": (f"z-slab x{world} (ghost plane; totals exchanged by "
                                 f"{'NVLink peer stores' if args.exchange == 'p2p' else 'NCCL all-gather'}; "
-                                f"{'equal plane runs' if balanced is None else 'plane runs balanced by surface'})"
+                                f"{slab_words(args.slabs, balanced)})"
                                 if world > 1 else "single GPU"),
                 "slab_bounds": balanced,
+                "slab_moves": moves or None,
                 "l2": (f"inputs larger than L2 (f32 slab {4.0 * local_nodes / 2**30:.2f} GiB per "
                        f"GPU vs 126 MB L2), no flush" if 4.0 * local_nodes > 126e6 * 2 else
                        "input smaller than 2x L2: numbers include L2 reuse between steps"),
@@ -769,6 +796,15 @@ def main():
     if world > 1:
         dist.destroy_process_group()
     return 0
+
+
+def slab_words(mode, bounds):
+    """How the node planes were split, for the JSON line."""
+    if bounds is None:
+        return "equal plane runs"
+    if mode == "surface":
+        return "plane runs balanced by surface"
+    return "plane runs moved toward equal measured device time per rank"
 
 
 def check_parity(args, tack, torch, dist, shape, isos, grid, all_counts, pts_buf, conn_buf,

@@ -90,6 +90,44 @@ def balanced_bounds(work, world, min_planes=2):
     return bounds
 
 
+def rebalanced_bounds(bounds, threshold_ms, busy_ms, damp=0.7, min_planes=2):
+    """Slab bounds moved toward equal device time per rank, from what each
+    rank measured on the current bounds: busy_ms[r] is rank r's device time
+    per step without the wait for the other ranks (threshold + count + emit),
+    threshold_ms[r] the part of it that scales with its node planes (the
+    threshold read).  A rank above the mean gives up planes, one below takes
+    them: (mean - busy) / (threshold time per plane) planes, times `damp`
+    (moving planes also moves surface, whose count and emit time the
+    threshold slope leaves out, so the full step would overshoot).  Returns
+    world + 1 increasing plane indices from 0 to the same last plane; every
+    run keeps at least `min_planes` planes.  Meant to be applied once or
+    twice; equal times return the same bounds."""
+    b = np.asarray(bounds, np.int64)
+    n = np.diff(b).astype(np.float64)
+    world = n.size
+    t = np.asarray(busy_ms, np.float64)
+    k1 = np.asarray(threshold_ms, np.float64)
+    if world < 1 or t.size != world or k1.size != world or np.any(n < 1):
+        raise ValueError(f"bad bounds {list(b)} or times for {world} ranks")
+    total = int(b[-1] - b[0])
+    if total < min_planes * world:
+        raise ValueError(f"cannot split {total} planes over {world} ranks")
+    per_plane = float(np.median(k1 / n))
+    if not np.isfinite(per_plane) or per_plane <= 0.0:
+        return [int(x) for x in b]
+    want = n + damp * (t.mean() - t) / per_plane
+    want = np.maximum(want, float(min_planes))
+    want *= total / want.sum()
+    c = np.concatenate([[0.0], np.cumsum(want)])
+    out = [int(b[0])]
+    for r in range(1, world):
+        k = int(b[0]) + int(round(c[r]))
+        k = min(max(k, out[-1] + min_planes), int(b[-1]) - (world - r) * min_planes)
+        out.append(k)
+    out.append(int(b[-1]))
+    return out
+
+
 def slab_bases(all_counts, rank):
     """Offsets of `rank`'s output within the global layout.
 

@@ -16,7 +16,8 @@ from datetime import timedelta
 import numpy as np
 import pytest
 
-from tack_b200.distributed import SlabPlan, assemble, balanced_bounds, gather_counts, slab_bases
+from tack_b200.distributed import (SlabPlan, assemble, balanced_bounds, gather_counts,
+                                   rebalanced_bounds, slab_bases)
 
 SHAPE = (23, 17, 29)          # cells; node planes along z: 30
 
@@ -130,6 +131,32 @@ def test_balanced_bounds():
     assert b[0] == 0 and b[-1] == 40 and all(b[i + 1] - b[i] >= 2 for i in range(4))
     with pytest.raises(ValueError):
         balanced_bounds(np.ones(7), 4)
+
+
+def test_rebalanced_bounds():
+    """Equal times keep the bounds; a slow rank gives planes to fast ones in
+    proportion to its excess over the threshold time per plane; the result
+    partitions the same planes with runs of at least two planes."""
+    eq = [0, 128, 256, 384, 513]
+    assert rebalanced_bounds(eq, [0.08] * 4, [0.16] * 4) == eq
+    # Rank 1 takes 10 us more than the others (152.5 us); 0.625 us per plane.
+    k1 = [0.080, 0.080, 0.080, 0.0806]
+    busy = [0.1525, 0.1625, 0.1525, 0.1525]
+    # Mean 155 us: rank 1 sheds 7.5 / 0.625 = 12 planes, the others take 4 each.
+    b = rebalanced_bounds(eq, k1, busy, damp=1.0)
+    assert b == [0, 132, 248, 380, 513]
+    # damp scales the move
+    assert rebalanced_bounds(eq, k1, busy, damp=0.5) == [0, 130, 252, 382, 513]
+    # a rank that is far too slow still keeps two planes, the runs still partition
+    b = rebalanced_bounds([0, 4, 8, 12, 16], [0.004] * 4, [10.0, 0.1, 0.1, 0.1])
+    assert b[0] == 0 and b[-1] == 16 and all(b[i + 1] - b[i] >= 2 for i in range(4))
+    # bounds not starting at zero keep their ends
+    b = rebalanced_bounds([10, 20, 30], [0.01, 0.01], [0.02, 0.03])
+    assert b[0] == 10 and b[-1] == 30 and b[1] > 20
+    with pytest.raises(ValueError):
+        rebalanced_bounds([0, 4, 8], [0.1], [0.1, 0.2])
+    with pytest.raises(ValueError):
+        rebalanced_bounds([0, 1, 3], [0.1, 0.1], [0.1, 0.1])
 
 
 @pytest.mark.parametrize("world", [2, 3, 5])
