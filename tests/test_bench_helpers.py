@@ -49,3 +49,17 @@ def test_install_reference_copies_the_two_source_trees(tmp_path, monkeypatch):
     assert not os.path.exists(dest / "tack-core" / "src" / "tack" / "__pycache__")
     with pytest.raises(FileNotFoundError):
         bench.install_reference(str(tmp_path / "missing"))
+
+
+def test_slab_split_arguments(monkeypatch):
+    """N>1 slabs default to measured balancing; --balance-slabs means the
+    surface split; the JSON wording names the split that ran."""
+    monkeypatch.setattr("sys.argv", ["bench.py"])
+    assert bench.parse_args().slabs == "measured"
+    monkeypatch.setattr("sys.argv", ["bench.py", "--balance-slabs"])
+    assert bench.parse_args().slabs == "surface"
+    monkeypatch.setattr("sys.argv", ["bench.py", "--slabs", "equal"])
+    assert bench.parse_args().slabs == "equal"
+    assert bench.slab_words("measured", None) == "equal plane runs"
+    assert "surface" in bench.slab_words("surface", [0, 3, 8])
+    assert "measured" in bench.slab_words("measured", [0, 3, 8])
